@@ -1,0 +1,442 @@
+"""Benchmark of the attention hot path: causal bf16 fwd + bwd, B=8 H=32 S=4096 D=128.
+
+One step = forward (with LSE) + backward (delta/clear, fused recompute
+kernel, dQ conversion) over this rank's (batch*head) slab of the BASELINE
+config-3 problem.  With N GPUs (torchrun, one process per GPU) the 256
+(batch, head) slabs are split evenly, with no collective on the data path
+("strong" scaling: the total problem is fixed).  Timing: per-step CUDA
+events on the launching stream after an L2 flush, K timed steps between a
+barrier + synchronize on both sides, max over ranks.
+
+``--impl reference`` times the reference's CPU path instead (fp32
+``F.scaled_dot_product_attention`` forward + autograd backward on the host
+cores, the reference's ``ref_fn``) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _entry in (ROOT / "triton-kernel-lab_b200", ROOT):
+    if str(_entry) not in sys.path:
+        sys.path.insert(0, str(_entry))
+
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: (batch, heads, seq, head_dim, dtype, causal, qk_std)
+    "c3": (8, 32, 4096, 128, torch.bfloat16, True, 1.0),
+    "c2": (4, 16, 1024, 64, torch.float16, False, 1.0),
+    "c4": (1, 32, 16384, 128, torch.bfloat16, True, 1.5),
+}
+L2_FLUSH_BYTES = 256 << 20
+THROTTLE_REASONS = {
+    0x1: "gpu_idle",
+    0x2: "applications_clocks_setting",
+    0x4: "sw_power_cap",
+    0x8: "hw_slowdown",
+    0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown",
+}
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"bf16_tflops": data["bf16_tflops"], "bf16_tflops_sustained": data["bf16_tflops_sustained"],
+                "hbm_gbs": data["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def fwd_flops(b: int, h: int, s: int, d: int, causal: bool) -> int:
+    """Reference FLOP model: 4 * B * H * pairs * D (flash_attention.py:737-747)."""
+    pairs = s * (s + 1) // 2 if causal else s * s
+    return 4 * b * h * pairs * d
+
+
+def bwd_flops(b: int, h: int, s: int, d: int, causal: bool) -> int:
+    """Algorithmic backward: 5 GEMMs = 2.5x the forward (recompute not credited)."""
+    return fwd_flops(b, h, s, d, causal) * 5 // 2
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons in the background during the timed region."""
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        query = "clocks.sm,clocks.max.sm,clocks_event_reasons.active"
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", "-i", str(self.index), f"--query-gpu={query}", "--format=csv,noheader,nounits"],
+                    capture_output=True, text=True, timeout=5, check=False,
+                ).stdout.strip()
+                sm, sm_max, reasons = (x.strip() for x in out.split(","))
+                self.samples.append((float(sm), float(sm_max), int(reasons, 16)))
+            except Exception:  # noqa: BLE001 - sampling is best-effort
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self) -> ClockSampler:
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        mask = 0
+        for _, _, r in self.samples:
+            mask |= r
+        reasons = [name for bit, name in THROTTLE_REASONS.items() if mask & bit and bit != 0x1]
+        return {
+            "sm_mhz": statistics.median(s for s, _, _ in self.samples),
+            "sm_max_mhz": max(m for _, m, _ in self.samples),
+            "reasons": reasons,
+            "samples": len(self.samples),
+        }
+
+
+def _dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def _make_inputs(shape: tuple[int, ...], dtype: torch.dtype, qk_std: float, seed: int, device) -> list[torch.Tensor]:
+    """Seeded synthetic Q, K, V, dO drawn on the device (no host round trip at this size)."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    q = (torch.randn(shape, generator=gen, device=device) * qk_std).to(dtype)
+    k = (torch.randn(shape, generator=gen, device=device) * qk_std).to(dtype)
+    v = torch.randn(shape, generator=gen, device=device).to(dtype)
+    do = torch.randn(shape, generator=gen, device=device).to(dtype)
+    return [q, k, v, do]
+
+
+def run_ours(args: argparse.Namespace) -> None:
+    from tklab import _native
+    from tklab.kernels.flash_attention import _NATIVE_DTYPE, attention_causal, attention_noncausal
+
+    rank, world, local_rank = _dist_env()
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=device)
+    b, h, s, d, dtype, causal, qk_std = CONFIGS[args.config]
+    bh_total = b * h
+    if bh_total % world:
+        raise SystemExit(f"{bh_total} (batch*head) slabs do not split over {world} ranks")
+    slab = bh_total // world
+    shape = (1, slab, s, d)  # this rank's contiguous slab of the flattened (B*H) axis
+    lib = _native.load()
+    q, k, v, do = _make_inputs(shape, dtype, qk_std, seed=args.seed + rank, device=device)
+    o = torch.empty_like(q)
+    lse = torch.empty((1, slab, s), dtype=torch.float32, device=device)
+    delta = torch.empty_like(lse)
+    dq_accum = torch.empty(shape, dtype=torch.float32, device=device)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    sp = int(stream.cuda_stream)
+    nd = _NATIVE_DTYPE[dtype]
+    scale = 1.0 / math.sqrt(d)
+    numel = q.numel()
+
+    def step(ev: list[torch.cuda.Event] | None) -> None:
+        def mark(i: int) -> None:
+            if ev is not None:
+                ev[i].record(stream)
+
+        mark(0)
+        _native.check(lib.tk_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                      1, slab, s, d, nd, int(causal), scale, sp), "fwd")
+        mark(1)
+        _native.check(lib.tk_attn_bwd_pre(o.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+                                          1, slab, s, d, nd, sp), "bwd_pre")
+        mark(2)
+        _native.check(lib.tk_attn_bwd_fused(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                            lse.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+                                            dk.data_ptr(), dv.data_ptr(), 1, slab, s, d, nd, int(causal),
+                                            scale, sp), "bwd")
+        mark(3)
+        _native.check(lib.tk_attn_dq_convert(dq_accum.data_ptr(), dq.data_ptr(), numel, nd, sp), "dq_convert")
+        mark(4)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step(None)
+    torch.cuda.synchronize(device)
+    status = _native.device_status(sp)
+    if status:
+        _native.check(status, "warm-up device status")
+
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(device)
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.__enter__()
+    for i in range(args.steps):
+        flush.zero_()  # write > L2 (126 MB) between timed steps, outside the step's events
+        step(events[i])
+    torch.cuda.synchronize(device)
+    if sampler:
+        sampler.__exit__()
+    if world > 1:
+        torch.distributed.barrier()
+    status = _native.device_status(sp)
+    if status:
+        _native.check(status, "timed-region device status")
+
+    per_kernel = [0.0] * 4
+    total_ms = 0.0
+    for ev in events:
+        for j in range(4):
+            per_kernel[j] += ev[j].elapsed_time(ev[j + 1])
+        total_ms += ev[0].elapsed_time(ev[4])
+    times = torch.tensor([total_ms] + per_kernel, dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
+    total_ms, k_fwd, k_pre, k_bwd, k_cvt = times.tolist()
+
+    # End-to-end through the public autograd API with host buffers.
+    e2e = None
+    if not args.no_e2e:
+        e2e = _e2e(args, attention_causal if causal else attention_noncausal, shape, dtype, qk_std, device, rank, world)
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_baseline(args.config, seconds=args.cpu_seconds)
+
+    if world > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        peaks = _peaks()
+        steps = args.steps
+        ff = fwd_flops(b, h, s, d, causal)
+        bf = bwd_flops(b, h, s, d, causal)
+        ms_per_step = total_ms / steps
+        value = (ff + bf) / (ms_per_step * 1e-3) / 1e12
+        # Dominant kernel: the one with the largest share of the step.
+        kernels = {"attn_fwd": (k_fwd / steps, ff / world), "attn_bwd_fused": (k_bwd / steps, bf / world)}
+        dom = max(kernels, key=lambda n: kernels[n][0])
+        dom_ms, dom_flops = kernels[dom]
+        achieved = dom_flops / (dom_ms * 1e-3) / 1e12
+        clocks = sampler.summary() if sampler else None
+        line = {
+            "metric": "attention fwd+bwd TFLOP/s (causal bf16 B=8 H=32 S=4096 D=128), aggregate over GPUs",
+            "value": round(value, 2),
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16" if dtype == torch.bfloat16 else "f16",
+            "data": "synthetic (seeded randn; Q,K std %.1f)" % qk_std,
+            "config": {
+                "workload": f"{args.config}: causal={causal} B={b} H={h} S={s} D={d} {str(dtype).split('.')[-1]}",
+                "global_batch": b,
+                "seq_len": s,
+                "heads": h,
+                "head_dim": d,
+                "parallelism": f"(batch*head) slabs {slab}/rank x {world} ranks, no collective",
+                "l2": "flushed: 256 MiB write before every timed step (outside its events)",
+            },
+            "fwd_tflops_per_gpu": round(ff / world / (k_fwd / steps * 1e-3) / 1e12, 2),
+            "bwd_tflops_per_gpu": round(bf / world / ((k_pre + k_bwd + k_cvt) / steps * 1e-3) / 1e12, 2),
+            "pct_peak_fwd": round(100 * ff / world / (k_fwd / steps * 1e-3) / 1e12 / peaks["bf16_tflops"], 2),
+            "pct_peak_bwd": round(
+                100 * bf / world / ((k_pre + k_bwd + k_cvt) / steps * 1e-3) / 1e12 / peaks["bf16_tflops"], 2),
+            "kernel_ms_per_step": {"attn_fwd": round(k_fwd / steps, 4), "attn_bwd_pre": round(k_pre / steps, 4),
+                                   "attn_bwd_fused": round(k_bwd / steps, 4), "dq_convert": round(k_cvt / steps, 4)},
+            "roofline": {
+                "kernel": dom,
+                "bound": "tensor",
+                "achieved": round(achieved, 2),
+                "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s",
+                "frac": round(achieved / peaks["bf16_tflops"], 4),
+                "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
+                "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
+                "traffic": args.traffic_bytes,
+            },
+            "gpu_launches": 4 * steps,
+            "gpu_launches_note": "per rank: fwd, bwd_pre, bwd_fused, dq_convert per step",
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def _e2e(args, attn, shape, dtype, qk_std, device, rank, world) -> dict | None:
+    """Public API, pinned host buffers in, results (O, dQ, dK, dV) back to the host, per step."""
+    b, h, s, d, _, causal, _ = CONFIGS[args.config]
+    host_in = [t.cpu().pin_memory() for t in _make_inputs(shape, dtype, qk_std, seed=args.seed + 100 + rank,
+                                                           device=device)]
+    host_out = [torch.empty(shape, dtype=dtype).pin_memory() for _ in range(4)]
+    stream = torch.cuda.current_stream(device)
+
+    def one() -> None:
+        q, k, v, do = (t.to(device, non_blocking=True) for t in host_in)
+        for t in (q, k, v):
+            t.requires_grad_(True)
+        out = attn(q, k, v)
+        grads = torch.autograd.grad(out, (q, k, v), grad_outputs=do)
+        for dst, src in zip(host_out, (out, *grads), strict=True):
+            dst.copy_(src.detach(), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        one()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.e2e_steps):
+        one()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    ms = torch.tensor([start.elapsed_time(end) / args.e2e_steps], dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms_step = float(ms.item())
+    flops = fwd_flops(b, h, s, d, causal) + bwd_flops(b, h, s, d, causal)
+    per_rank_bytes = 4 * math.prod(shape) * torch.empty((), dtype=dtype).element_size()
+    return {
+        "value": round(flops / (ms_step * 1e-3) / 1e12, 2),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms_step, 3),
+        "h2d_bytes_per_step": per_rank_bytes * world,
+        "d2h_bytes_per_step": per_rank_bytes * world,
+        "path": "tklab.kernels.flash_attention.attention_causal + torch.autograd.grad, pinned host buffers",
+        "steps": args.e2e_steps,
+    }
+
+
+def _cpu_slab_step(shape, dtype, causal, qk_std, seed) -> float:
+    from oracle.attention_oracle import sdpa_backward
+
+    gen = torch.Generator().manual_seed(seed)
+    q = (torch.randn(shape, generator=gen) * qk_std).to(dtype)
+    k = (torch.randn(shape, generator=gen) * qk_std).to(dtype)
+    v = torch.randn(shape, generator=gen).to(dtype)
+    do = torch.randn(shape, generator=gen).to(dtype)
+    t0 = time.perf_counter()
+    sdpa_backward(q, k, v, do, causal=causal)
+    return time.perf_counter() - t0
+
+
+def _cpu_baseline(config: str, seconds: float) -> dict:
+    """The reference's CPU path (fp32 SDPA fwd + autograd bwd) on a bounded sample: one (b, h) slab per rep."""
+    b, h, s, d, dtype, causal, qk_std = CONFIGS[config]
+    torch.set_num_threads(os.cpu_count() or 1)
+    shape = (1, 1, s, d)
+    _cpu_slab_step(shape, dtype, causal, qk_std, 0)  # warm-up
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 3:
+        times.append(_cpu_slab_step(shape, dtype, causal, qk_std, len(times) + 1))
+    per_slab = statistics.median(times)
+    flops = (fwd_flops(1, 1, s, d, causal) + bwd_flops(1, 1, s, d, causal))
+    return {
+        "value": round(flops / per_slab / 1e12, 4),
+        "unit": "TFLOP/s",
+        "cores": torch.get_num_threads(),
+        "kind": "reference",
+        "sample": f"{len(times)} reps of one (b,h) slab ({s}x{d}, causal={causal}) fwd+bwd; median {per_slab:.3f} s",
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return
+    b, h, s, d, dtype, causal, qk_std = CONFIGS[args.config]
+    torch.set_num_threads(os.cpu_count() or 1)
+    shape = (1, 1, s, d)
+    for i in range(args.warmup):
+        _cpu_slab_step(shape, dtype, causal, qk_std, 1000 + i)
+    total = 0.0
+    for i in range(args.steps):
+        total += _cpu_slab_step(shape, dtype, causal, qk_std, i)
+    per_step = total / args.steps
+    flops = fwd_flops(1, 1, s, d, causal) + bwd_flops(1, 1, s, d, causal)
+    value = flops / per_step / 1e12
+    line = {
+        "impl": "reference",
+        "metric": "attention fwd+bwd TFLOP/s (causal bf16 B=8 H=32 S=4096 D=128), aggregate over GPUs",
+        "value": round(value, 4),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_step * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded randn)",
+        "config": {"workload": f"{args.config}: one (b,h) slab per step of B={b} H={h} S={s} D={d}",
+                   "global_batch": b, "seq_len": s},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "reference",
+                         "sample": f"one (b,h) slab ({s}x{d}) fp32 SDPA fwd+autograd bwd per step"},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--config", choices=tuple(CONFIGS), default="c3")
+    parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--e2e-steps", type=int, default=5)
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--traffic-bytes", type=float, default=None,
+                        help="ncu dram bytes per launch of the dominant kernel, if captured")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * tklab_attn.h — C ABI of the B200 (sm_100a) flash-attention library
+ * (libtklab_attn.so).  Plain pointers, sizes and a CUDA stream handle; no
+ * PyTorch types.  Every entry point validates its arguments, launches
+ * asynchronously on `stream` (a cudaStream_t, NULL = legacy default stream)
+ * and returns a status code (TK_OK = 0).  Errors detected on the device
+ * (a bounded wait that ran out) are recorded in a per-device status word
+ * read by tk_attn_device_status().
+ *
+ * Layout contract (same as the reference module): Q, K, V, O, dO, dQ, dK,
+ * dV are contiguous (batch, heads, seq, head_dim) tensors of one 16-bit
+ * type; the log-sum-exp and delta buffers are contiguous fp32
+ * (batch, heads, seq).  The log-sum-exp is base 2 and includes the softmax
+ * scale: lse = log2(sum_n exp2(scale * log2(e) * q.k_n)).
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   tk_attn_fwd         src/tklab/kernels/flash_attention.py:296-347
+ *                       (_launch_forward and its launch of
+ *                        _flash_attention_forward_kernel, :120-264)
+ *   tk_attn_bwd_pre     src/tklab/kernels/flash_attention.py:560-569
+ *                       (_attn_bwd_preprocess_kernel launch, :368-395)
+ *   tk_attn_bwd         src/tklab/kernels/flash_attention.py:570-606
+ *                       (_attn_bwd_dkdv_kernel :398-466 and
+ *                        _attn_bwd_dq_kernel :469-533 launches)
+ *   tk_attn_bwd_fused / tk_attn_dq_convert
+ *                       the two launches of tk_attn_bwd, exposed separately
+ *   tk_attn_bwd_workspace_bytes
+ *                       the fp32 dQ accumulator size; the reference needs
+ *                       no workspace because its dQ pass recomputes P
+ *                       (src/tklab/kernels/flash_attention.py:589-606)
+ */
+#ifndef TKLAB_ATTN_H_
+#define TKLAB_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TK_API __attribute__((visibility("default")))
+#else
+#define TK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type of Q/K/V/O/dO/dQ/dK/dV. */
+#define TK_DTYPE_F16 0
+#define TK_DTYPE_BF16 1
+
+/* Status codes. */
+#define TK_OK 0
+#define TK_ERR_INVALID_ARGUMENT 1
+#define TK_ERR_UNSUPPORTED 2
+#define TK_ERR_MISALIGNED 3
+#define TK_ERR_LAUNCH 4
+#define TK_ERR_TENSOR_MAP 5
+#define TK_ERR_DEVICE_TIMEOUT 6 /* low byte; bits 8.. carry the wait site */
+#define TK_ERR_NO_DRIVER 7
+#define TK_ERR_TOO_LARGE 8
+
+/* Forward attention.  o receives softmax(scale * q k^T) v (causal: key n
+ * attends query m only when n <= m).  lse may be NULL; otherwise it
+ * receives the base-2 log-sum-exp of every query row.  head_dim must be 64
+ * or 128; q, k, v, o must be 16-byte aligned. */
+TK_API int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
+                int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                void* stream);
+
+/* Backward preprocessing: delta[b,h,m] = sum_d o[b,h,m,d] * d_o[b,h,m,d]
+ * (fp32), and, when dq_accum is not NULL, the fp32 dQ accumulator
+ * (batch*heads*seq*head_dim floats, 16-byte aligned) cleared to zero. */
+TK_API int tk_attn_bwd_pre(const void* o, const void* d_o, float* delta, float* dq_accum, int64_t batch,
+                    int64_t heads, int64_t seq, int64_t head_dim, int dtype, void* stream);
+
+/* Backward attention from the saved lse and the delta of tk_attn_bwd_pre.
+ * dq_accum must hold zeros on entry (tk_attn_bwd_pre clears it); it is used
+ * as an fp32 workspace and then converted into dq.  dk and dv are written
+ * directly.  All of q, k, v, d_o, dq, dk, dv must be 16-byte aligned. */
+TK_API int tk_attn_bwd(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                const float* delta, float* dq_accum, void* dq, void* dk, void* dv, int64_t batch,
+                int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                void* stream);
+
+/* The two launches of tk_attn_bwd, for callers that schedule them apart:
+ * tk_attn_bwd_fused runs the fused recompute kernel (dK and dV written,
+ * scaled dQ contributions added into dq_accum), tk_attn_dq_convert turns the
+ * n-element fp32 accumulator into dq (n a multiple of 8). */
+TK_API int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d_o,
+                             const float* lse, const float* delta, float* dq_accum, void* dk,
+                             void* dv, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                             int dtype, int causal, float scale, void* stream);
+TK_API int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream);
+
+/* Bytes of the fp32 dQ accumulator tk_attn_bwd needs (0 on bad sizes). */
+TK_API size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);
+
+/* Synchronise `stream`, then read and clear the current device's status
+ * word (TK_OK when no kernel reported an error since the last read). */
+TK_API int tk_attn_device_status(int* status_out, void* stream);
+
+/* Upper bound, in nanoseconds, of every wait inside the kernels (default
+ * 2e9).  A wait that runs out records TK_ERR_DEVICE_TIMEOUT and the kernel
+ * drains and exits instead of hanging. */
+TK_API int tk_attn_set_wait_timeout_ns(unsigned long long timeout_ns);
+
+/* Launch a one-CTA kernel that waits on a barrier nothing ever arrives at,
+ * bounded by timeout_ns: exercises the device-timeout path without any
+ * fault.  The status word then reads TK_ERR_DEVICE_TIMEOUT. */
+TK_API int tk_attn_selftest_wait_timeout(unsigned long long timeout_ns, void* stream);
+
+/* Diagnostic: one 128 x n x 128 tcgen05 product in the operand form `mode`
+ * uses inside the attention kernels, written as fp32 row-major c.
+ *   mode 0: c[128][128] = a[128][128] . b[128][128]^T   (both K-major)
+ *   mode 1: c[128][n]   = a[128][128] . b[128][n]       (a read from TMEM)
+ *   mode 2: c[128][n]   = a[128][128]^T . b[128][n]     (both MN-major)
+ *   mode 3: c[128][n]   = a[128][128] . b[128][n]       (a K-major, b MN-major)
+ * n is 64 or 128 (ignored for mode 0).  No counterpart in the reference:
+ * it pins the operand conventions the kernels rely on. */
+TK_API int tk_attn_diag_umma(const void* a, const void* b, float* c, int mode, int n, int dtype,
+                      void* stream);
+
+/* Human-readable name of a status code. */
+TK_API const char* tk_attn_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TKLAB_ATTN_H_ */

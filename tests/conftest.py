@@ -1,0 +1,53 @@
+"""Shared pytest configuration.
+
+Puts the package directory (``triton-kernel-lab_b200``, holding ``tklab``) and
+the repository root (holding ``oracle``) on ``sys.path`` — the equivalent of
+the reference's ``pythonpath = ["src", "."]`` — and registers the markers.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+for entry in (ROOT / "triton-kernel-lab_b200", ROOT):
+    if str(entry) not in sys.path:
+        sys.path.insert(0, str(entry))
+
+GOLDEN_DIR = ROOT / "tests" / "golden"
+
+
+def pytest_configure(config: pytest.Config) -> None:
+    config.addinivalue_line("markers", "gpu: requires a CUDA GPU (B200, sm_100a)")
+
+
+def golden_cases() -> list[str]:
+    """Names of the committed golden fixtures."""
+    return sorted(path.stem for path in GOLDEN_DIR.glob("*.npz"))
+
+
+def load_golden(name: str) -> dict[str, object]:
+    """Load one fixture: 16-bit tensors are rebuilt bit-exactly from their stored bits."""
+    import torch
+
+    with np.load(GOLDEN_DIR / f"{name}.npz") as data:
+        raw = {key: data[key] for key in data.files}
+    dtype = getattr(torch, str(raw.pop("dtype")))
+    out: dict[str, object] = {
+        "dtype": dtype,
+        "causal": bool(raw.pop("causal")),
+        "seed": int(raw.pop("seed")),
+    }
+    for key, value in raw.items():
+        if key.endswith("_bits"):
+            base = key[: -len("_bits")]
+            bits = torch.from_numpy(value.view(np.int16).copy())
+            tensor_dtype = dtype if base in ("q", "k", "v", "do") else torch.float16
+            out[base] = bits.view(tensor_dtype)
+        else:
+            out[key] = torch.from_numpy(value.copy())
+    return out

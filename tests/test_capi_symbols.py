@@ -1,0 +1,75 @@
+"""CPU: the C-ABI library loads and exports every entry point of include/tklab_attn.h.
+
+Only calls that return before touching a GPU are made here (argument
+validation and pure size arithmetic).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from tklab import _native
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "tklab_attn.h"
+
+
+def _declared() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^TK_API\s+[\w\s\*]+?\b(tk_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_the_documented_entry_points() -> None:
+    declared = _declared()
+    assert {"tk_attn_fwd", "tk_attn_bwd_pre", "tk_attn_bwd"} <= declared
+    assert declared == set(_native.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol() -> None:
+    lib = _native.load()
+    for name in _declared():
+        assert isinstance(getattr(lib, name), ctypes._CFuncPtr), name
+
+
+def test_workspace_size_arithmetic() -> None:
+    lib = _native.load()
+    assert lib.tk_attn_bwd_workspace_bytes(8, 32, 4096, 128) == 8 * 32 * 4096 * 128 * 4
+    assert lib.tk_attn_bwd_workspace_bytes(0, 32, 4096, 128) == 0
+
+
+@pytest.mark.parametrize(
+    ("kwargs", "status"),
+    [
+        ({"q": None}, 1),
+        ({"head_dim": 96}, 2),
+        ({"head_dim": 256}, 2),
+        ({"dtype": 7}, 2),
+        ({"seq": 0}, 1),
+        ({"batch": -1}, 1),
+        ({"scale": 0.0}, 1),
+        ({"q": 0x1008}, 3),
+    ],
+)
+def test_forward_rejects_bad_arguments_before_launch(kwargs: dict, status: int) -> None:
+    args = {"q": 0x1000, "k": 0x2000, "v": 0x3000, "o": 0x4000, "lse": None, "batch": 1, "heads": 2,
+            "seq": 128, "head_dim": 64, "dtype": 0, "causal": 0, "scale": 0.125, "stream": None}
+    args.update(kwargs)
+    assert _native.load().tk_attn_fwd(*args.values()) == status
+
+
+def test_backward_rejects_missing_workspace() -> None:
+    lib = _native.load()
+    rc = lib.tk_attn_bwd(0x1000, 0x2000, 0x3000, 0x4000, 0x5000, 0x6000, None, 0x7000, 0x8000, 0x9000,
+                         1, 2, 128, 64, 0, 1, 0.125, None)
+    assert rc == 1
+
+
+def test_status_strings() -> None:
+    assert _native.status_string(0) == "ok"
+    assert _native.status_string(6) == "device wait timed out"
+    assert _native.status_string(6 | (3 << 8)) == "device wait timed out"
+    with pytest.raises(RuntimeError, match="wait site 3"):
+        _native.check(6 | (3 << 8), "probe")

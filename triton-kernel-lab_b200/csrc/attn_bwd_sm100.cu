@@ -1,0 +1,443 @@
+// Flash-attention backward for sm_100a (B200): one fused recompute kernel that
+// produces dK and dV for a 128-key tile and streams dQ contributions into an
+// fp32 accumulator, all five contractions on tcgen05 with TMEM accumulators.
+//
+// Semantics follow the reference kernels `_attn_bwd_dkdv_kernel` and
+// `_attn_bwd_dq_kernel` (src/tklab/kernels/flash_attention.py:398-533):
+//   P  = exp2(scale*log2(e) * Q.K^T - LSE2)     (LSE2 = base-2 log-sum-exp)
+//   dV += P^T dO            dP = dO V^T        dS = P * (dP - delta)
+//   dK += dS^T Q (times scale)                 dQ += dS K (times scale)
+// with P and dS rounded to the input dtype for their products (:459-462,530),
+// causal blocks below the diagonal skipped (:438, :513) and the diagonal and
+// ragged tails masked (:454-457, :523-526).  The reference runs dK/dV and dQ
+// as two kernels that both recompute P (14 N^2 d MMA flops); here dQ is
+// produced by the same CTA (10 N^2 d) and reduced across key tiles with
+// 128-bit fp32 atomics.
+//
+// One CTA owns a 128-key tile (K, V resident in smem) of one (batch, head)
+// and walks 128-query steps.  The transposed products are computed directly
+// (S^T = K Q^T, dP^T = V dO^T) so TMEM lane n holds key n:
+//   warp 0      producer: TMA for K, V, Q_i, dO_i; plain loads of LSE/delta
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
+//   warps 2..5  "dS warps": thread n owns key n; P^T and dS^T for all 128
+//               queries of a step (P^T back to TMEM for the dV MMA, dS^T to
+//               smem for the dK and dQ MMAs); dV epilogue
+//   warps 6..9  "dQ warps": thread m owns query m of the step; read dQ from
+//               TMEM and add it into the fp32 accumulator; dK epilogue
+// TMEM columns: dV [0,D) dK [D,2D) S^T/P^T [2D,2D+128) dP^T [2D+128,2D+256)
+// dQ after dP^T when it fits (D=64), otherwise aliased onto dP^T (D=128),
+// which the next step's dP^T MMA reclaims only once dQ has been read out.
+#include "attn_launch.h"
+#include "sm100_primitives.cuh"
+
+namespace tk {
+namespace {
+
+template <int D>
+struct BwdCfg {
+  static constexpr int kQStages = 2;
+  static constexpr int kTileBytes = kTileRows * D * 2;
+  static constexpr int kKOff = 0;
+  static constexpr int kVOff = kKOff + kTileBytes;
+  static constexpr int kQOff = kVOff + kTileBytes;
+  static constexpr int kDOOff = kQOff + kQStages * kTileBytes;
+  static constexpr int kDSOff = kDOOff + kQStages * kTileBytes;
+  static constexpr int kDSBytes = kTileRows * kTileRows * 2;
+  static constexpr int kLseOff = kDSOff + kDSBytes;        // float[2][128]
+  static constexpr int kDeltaOff = kLseOff + 2 * 128 * 4;  // float[2][128]
+  static constexpr int kBarOff = kDeltaOff + 2 * 128 * 4;
+  // kv_full, q_full[QS], do_full[QS], qdo_empty[QS], ld_full[2], ld_empty[2],
+  // s_full, dp_full, ds_ready, ds_empty, dq_full, dq_empty, dkdv_done
+  static constexpr int kNumBars = 1 + 3 * kQStages + 4 + 7;
+  static constexpr int kCtlOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kCtlOff + 64;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColDV = 0;
+  static constexpr uint32_t kColDK = D;
+  static constexpr uint32_t kColS = 2 * D;
+  static constexpr uint32_t kColDP = 2 * D + 128;
+  static constexpr bool kDqAliased = (2 * D + 256 + D) > 512;
+  static constexpr uint32_t kColDQ = kDqAliased ? kColDP : 2 * D + 256;
+};
+
+constexpr int kBwdThreads = 320;
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaControl* ctl,
+                                          uint64_t timeout_ns, int* status, int site) {
+  const bool ok = mbar_wait(bar, parity, ctl, timeout_ns, status, site);
+  return __all_sync(0xffffffffu, ok);
+}
+
+// Stage one TMEM row (D fp32 values, times `mul`) as dtype into a swizzled
+// 128-row tile in smem, row `r`.
+template <int D, bool kBf16>
+__device__ __forceinline__ void stage_row(uint32_t t_row, uint8_t* tile, int r, float mul) {
+#pragma unroll
+  for (int cb = 0; cb < D / 32; ++cb) {
+    uint32_t v[32];
+    tmem_ld32(t_row + cb * 32, v);
+    tmem_wait_ld();
+    reg_fence(v);
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint4 w;
+      w.x = pack2<kBf16>(__uint_as_float(v[ch * 8 + 0]) * mul, __uint_as_float(v[ch * 8 + 1]) * mul);
+      w.y = pack2<kBf16>(__uint_as_float(v[ch * 8 + 2]) * mul, __uint_as_float(v[ch * 8 + 3]) * mul);
+      w.z = pack2<kBf16>(__uint_as_float(v[ch * 8 + 4]) * mul, __uint_as_float(v[ch * 8 + 5]) * mul);
+      w.w = pack2<kBf16>(__uint_as_float(v[ch * 8 + 6]) * mul, __uint_as_float(v[ch * 8 + 7]) * mul);
+      *reinterpret_cast<uint4*>(tile + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
+    }
+  }
+}
+
+template <int D, bool kBf16>
+__global__ void __launch_bounds__(kBwdThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                    const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                    const float* __restrict__ lse, const float* __restrict__ delta,
+                    float* __restrict__ dq_accum, int S, int BH, int n_tiles, int causal, float scale,
+                    float scale_log2, unsigned long long timeout_ns, int* status) {
+  using C = BwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicCAS(status, kOk, kErrMisaligned);
+    return;
+  }
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Key tiles with the most query steps (smallest index under a causal mask)
+  // launch first.
+  const int jn = static_cast<int>(blockIdx.x) / BH;
+  const int bh = static_cast<int>(blockIdx.x) % BH;
+  const int n0 = jn * kTileRows;
+  const int i_start = causal ? jn : 0;
+  const int n_steps = n_tiles - i_start;
+
+  uint8_t* sK = smem + C::kKOff;
+  uint8_t* sV = smem + C::kVOff;
+  uint8_t* sQ = smem + C::kQOff;
+  uint8_t* sDO = smem + C::kDOOff;
+  uint8_t* sDS = smem + C::kDSOff;
+  float* sLse = reinterpret_cast<float*>(smem + C::kLseOff);
+  float* sDelta = reinterpret_cast<float*>(smem + C::kDeltaOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* kv_full = bars;
+  uint64_t* q_full = bars + 1;
+  uint64_t* do_full = q_full + C::kQStages;
+  uint64_t* qdo_empty = do_full + C::kQStages;
+  uint64_t* ld_full = qdo_empty + C::kQStages;
+  uint64_t* ld_empty = ld_full + 2;
+  uint64_t* s_full = ld_empty + 2;
+  uint64_t* dp_full = s_full + 1;
+  uint64_t* ds_ready = dp_full + 1;
+  uint64_t* ds_empty = ds_ready + 1;
+  uint64_t* dq_full = ds_empty + 1;
+  uint64_t* dq_empty = dq_full + 1;
+  uint64_t* dkdv_done = dq_empty + 1;
+  CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < C::kQStages; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&do_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&ld_full[i], 32);
+      mbar_init(&ld_empty[i], 4);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(ds_ready, 4);
+    mbar_init(ds_empty, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(dkdv_done, 1);
+    ctl->abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tm_q);
+    tma_prefetch_map(&tm_k);
+    tma_prefetch_map(&tm_v);
+    tma_prefetch_map(&tm_do);
+    tma_prefetch_map(&tm_dk);
+    tma_prefetch_map(&tm_dv);
+  }
+  if (warp == 1) tmem_alloc(&ctl->tmem_base, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  const size_t row_base = static_cast<size_t>(bh) * S;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) {
+        tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
+        tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
+      }
+    }
+    for (int it = 0; it < n_steps; ++it) {
+      const int m0 = (i_start + it) * kTileRows;
+      const int st = it % C::kQStages;
+      const uint32_t ph = (it / C::kQStages) & 1;
+      if (!warp_wait(&qdo_empty[st], ph ^ 1, ctl, timeout_ns, status, 1)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&q_full[st], C::kTileBytes);
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b)
+          tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, m0, bh);
+        mbar_arrive_expect_tx(&do_full[st], C::kTileBytes);
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b)
+          tma_load_3d(sDO + st * C::kTileBytes + b * kBlockBytes, &tm_do, &do_full[st], b * 64, m0, bh);
+      }
+      // LSE / delta for this query step.  Padded queries get LSE = +inf so
+      // their probabilities are exactly zero.
+      const int lb = it & 1;
+      if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = e * 32 + lane;
+        const int mg = m0 + q;
+        const bool valid = mg < S;
+        sLse[lb * 128 + q] = valid ? lse[row_base + mg] : INFINITY;
+        sDelta[lb * 128 + q] = valid ? delta[row_base + mg] : 0.0f;
+      }
+      mbar_arrive(&ld_full[lb]);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t fmt = kBf16 ? 1u : 0u;
+      const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
+      const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
+      const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
+      const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sDSa = smem_u32(sDS);
+      bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 3);
+      for (int it = 0; ok && it < n_steps; ++it) {
+        const int st = it % C::kQStages;
+        const uint32_t ph = (it / C::kQStages) & 1;
+        const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
+        const uint32_t sDOa = smem_u32(sDO + st * C::kTileBytes);
+        // S^T = K Q^T
+        if (!(ok = mbar_wait(&q_full[st], ph, ctl, timeout_ns, status, 4))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem + C::kColS, sdesc_kmajor(sKa, kTileRows, kk * 16),
+                  sdesc_kmajor(sQa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        // dP^T = V dO^T
+        if (!(ok = mbar_wait(&do_full[st], ph, ctl, timeout_ns, status, 5))) break;
+        if (C::kDqAliased && it > 0) {
+          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6))) break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(tmem + C::kColDP, sdesc_kmajor(sVa, kTileRows, kk * 16),
+                  sdesc_kmajor(sDOa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit(dp_full);
+        // P^T (TMEM) and dS^T (smem) from the dS warps
+        if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 7))) break;
+        tc_fence_after();
+        // dV += P^T dO
+#pragma unroll
+        for (int kk = 0; kk < kTileRows / 16; ++kk)
+          umma_ts(tmem + C::kColDV, tmem + C::kColS + kk * 8, sdesc_mnmajor(sDOa, kTileRows, kk * 16),
+                  idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+        // dK += dS^T Q
+#pragma unroll
+        for (int kk = 0; kk < kTileRows / 16; ++kk)
+          umma_ss(tmem + C::kColDK, sdesc_kmajor(sDSa, kTileRows, kk * 16),
+                  sdesc_mnmajor(sQa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&qdo_empty[st]);
+        // dQ = dS K
+        if (!C::kDqAliased && it > 0) {
+          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 8))) break;
+        }
+#pragma unroll
+        for (int kk = 0; kk < kTileRows / 16; ++kk)
+          umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
+                  sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(ds_empty);
+      }
+      if (ok) umma_commit(dkdv_done);
+    }
+  } else if (warp < 6) {
+    // ---------------- dS warps: thread t owns key n0 + t ----------------
+    const int q4 = warp & 3;
+    const int t = q4 * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const bool key_ok = (n0 + t) < S;
+    bool ok = true;
+    for (int it = 0; it < n_steps; ++it) {
+      const int i = i_start + it;
+      const int lb = it & 1;
+      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 9))) break;
+      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 10))) break;
+      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 11))) break;
+      if (it > 0) {
+        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 12))) break;
+      }
+      tc_fence_after();
+      const bool diag = causal && (i == jn);
+      const float* lse_s = sLse + lb * 128;
+      const float* del_s = sDelta + lb * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dpv[32];
+        tmem_ld32(t_lane + C::kColS + c * 32, sv);
+        tmem_ld32(t_lane + C::kColDP + c * 32, dpv);
+        tmem_wait_ld();
+        reg_fence(sv);
+        reg_fence(dpv);
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const int q = c * 32 + e;
+          float p0 = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse_s[q]));
+          float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), scale_log2, -lse_s[q + 1]));
+          if (diag) {
+            if (q < t) p0 = 0.0f;
+            if (q + 1 < t) p1 = 0.0f;
+          }
+          if (!key_ok) {
+            p0 = 0.0f;
+            p1 = 0.0f;
+          }
+          const float d0 = p0 * (__uint_as_float(dpv[e]) - del_s[q]);
+          const float d1 = p1 * (__uint_as_float(dpv[e + 1]) - del_s[q + 1]);
+          pp[e >> 1] = pack2<kBf16>(p0, p1);
+          dd[e >> 1] = pack2<kBf16>(d0, d1);
+        }
+        tmem_st16(t_lane + C::kColS + c * 16, pp);
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint4 v = make_uint4(dd[w * 4 + 0], dd[w * 4 + 1], dd[w * 4 + 2], dd[w * 4 + 3]);
+          *reinterpret_cast<uint4*>(sDS + swz_offset(t, c * 32 + w * 8, kTileRows)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&ld_empty[lb]);
+        mbar_arrive(ds_ready);
+      }
+    }
+    // dV epilogue (staged through Q stage 0, stored by TMA; rows >= S are
+    // clipped by the tensor map bounds).
+    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 13);
+    if (ok) {
+      tc_fence_after();
+      stage_row<D, kBf16>(t_lane + C::kColDV, sQ, t, 1.0f);
+      fence_proxy_async_smem();
+    }
+    named_barrier_sync(1, 128);
+    if (warp == 2 && lane == 0 && !ctl->abort) {
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) tma_store_3d(&tm_dv, sQ + b * kBlockBytes, b * 64, n0, bh);
+      tma_store_commit();
+      tma_store_wait_read_all();
+    }
+  } else {
+    // ---------------- dQ warps: thread r owns query m0 + r ----------------
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    bool ok = true;
+    for (int it = 0; it < n_steps; ++it) {
+      const int mg = (i_start + it) * kTileRows + r;
+      if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 14))) break;
+      tc_fence_after();
+      uint32_t v[D / 32][32];
+#pragma unroll
+      for (int cb = 0; cb < D / 32; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int cb = 0; cb < D / 32; ++cb) reg_fence(v[cb]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      if (mg < S) {
+        float4* dst = reinterpret_cast<float4*>(dq_accum + (row_base + mg) * D);
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) {
+#pragma unroll
+          for (int f = 0; f < 8; ++f) {
+            const float4 add = make_float4(__uint_as_float(v[cb][4 * f + 0]) * scale,
+                                           __uint_as_float(v[cb][4 * f + 1]) * scale,
+                                           __uint_as_float(v[cb][4 * f + 2]) * scale,
+                                           __uint_as_float(v[cb][4 * f + 3]) * scale);
+            atomicAdd(dst + cb * 8 + f, add);
+          }
+        }
+      }
+    }
+    // dK epilogue (staged through dO stage 0).
+    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 13);
+    if (ok) {
+      tc_fence_after();
+      stage_row<D, kBf16>(t_lane + C::kColDK, sDO, r, scale);
+      fence_proxy_async_smem();
+    }
+    named_barrier_sync(2, 128);
+    if (warp == 6 && lane == 0 && !ctl->abort) {
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) tma_store_3d(&tm_dk, sDO + b * kBlockBytes, b * 64, n0, bh);
+      tma_store_commit();
+      tma_store_wait_read_all();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <int D, bool kBf16>
+int launch_bwd_t(const BwdArgs& a) {
+  using C = BwdCfg<D>;
+  static_assert(C::kSmemBytes <= 232448, "backward shared memory exceeds the sm_100 limit");
+  auto kern = attn_bwd_kernel<D, kBf16>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return kErrLaunch;
+    attr_set[dev] = true;
+  }
+  const int n_tiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
+  const long long grid = static_cast<long long>(n_tiles) * a.BH;
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, C::kSmemBytes, a.stream>>>(
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, *a.tm_dk, *a.tm_dv, a.lse, a.delta, a.dq_accum,
+      static_cast<int>(a.S), static_cast<int>(a.BH), n_tiles, a.causal, a.scale, a.scale_log2,
+      a.timeout_ns, a.status);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace
+
+int launch_attn_bwd(const BwdArgs& a) {
+  if (a.D == 64) return a.bf16 ? launch_bwd_t<64, true>(a) : launch_bwd_t<64, false>(a);
+  if (a.D == 128) return a.bf16 ? launch_bwd_t<128, true>(a) : launch_bwd_t<128, false>(a);
+  return kErrUnsupported;
+}
+
+}  // namespace tk

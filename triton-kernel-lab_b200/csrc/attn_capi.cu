@@ -1,0 +1,246 @@
+// C ABI of libtklab_attn.so (declared in include/tklab_attn.h): argument
+// validation, TMA tensor-map encoding and kernel dispatch.  Host code only
+// besides the per-device status word.
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cmath>
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/tklab_attn.h"
+#include "attn_launch.h"
+#include "sm100_primitives.cuh"
+
+namespace {
+
+// Device status word: kernels record the first error they hit here.
+__device__ int g_tk_status_word = 0;
+
+constexpr int kMaxDevices = 64;
+int* g_status_ptr[kMaxDevices] = {};
+std::mutex g_mu;
+unsigned long long g_timeout_ns = 2000000000ull;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int status_ptr(int** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return tk::kErrNoDriver;
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_tk_status_word) != cudaSuccess) return tk::kErrNoDriver;
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  *out = g_status_ptr[dev];
+  return tk::kOk;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_shape(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype) {
+  if (batch <= 0 || heads <= 0 || seq <= 0) return tk::kErrInvalidArgument;
+  if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
+  if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
+  const int64_t bh = batch * heads;
+  if (bh > INT_MAX || seq > INT_MAX) return tk::kErrTooLarge;
+  const int64_t tiles = (seq + 127) / 128;
+  if (tiles * bh > INT_MAX) return tk::kErrTooLarge;
+  return tk::kOk;
+}
+
+// 3-D map over a contiguous (B*H, S, D) 16-bit tensor: box {64, 128, 1},
+// 128-byte swizzle, zero fill outside the tensor (ragged S tails).
+int make_map(CUtensorMap* map, const void* base, int64_t bh, int64_t seq, int64_t head_dim,
+             int dtype) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return tk::kErrNoDriver;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq),
+                        static_cast<cuuint64_t>(bh)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * 2),
+                           static_cast<cuuint64_t>(seq * head_dim * 2)};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map,
+                  dtype == TK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                  3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? tk::kOk : tk::kErrTensorMap;
+}
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+}  // namespace
+
+extern "C" {
+
+int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
+                int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return tk::kErrMisaligned;
+  if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u)) return tk::kErrMisaligned;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  const int64_t bh = batch * heads;
+  CUtensorMap mq, mk, mv, mo;
+  if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mo, o, bh, seq, head_dim, dtype)) return rc;
+  tk::FwdArgs a{&mq, &mk, &mv, &mo, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16,
+                causal ? 1 : 0, scale * kLog2e, g_timeout_ns, status,
+                static_cast<cudaStream_t>(stream)};
+  return tk::launch_attn_fwd(a);
+}
+
+int tk_attn_bwd_pre(const void* o, const void* d_o, float* delta, float* dq_accum, int64_t batch,
+                    int64_t heads, int64_t seq, int64_t head_dim, int dtype, void* stream) {
+  if (o == nullptr || d_o == nullptr || delta == nullptr) return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (!aligned16(o) || !aligned16(d_o)) return tk::kErrMisaligned;
+  if (reinterpret_cast<uintptr_t>(delta) & 3u) return tk::kErrMisaligned;
+  if (dq_accum != nullptr && !aligned16(dq_accum)) return tk::kErrMisaligned;
+  tk::BwdPreArgs a{o, d_o, delta, dq_accum, batch * heads, seq, head_dim, dtype == TK_DTYPE_BF16,
+                   static_cast<cudaStream_t>(stream)};
+  return tk::launch_attn_bwd_pre(a);
+}
+
+int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                      const float* delta, float* dq_accum, void* dk, void* dv, int64_t batch,
+                      int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                      void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || d_o == nullptr || lse == nullptr ||
+      delta == nullptr || dq_accum == nullptr || dk == nullptr || dv == nullptr)
+    return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(d_o) || !aligned16(dk) ||
+      !aligned16(dv) || !aligned16(dq_accum))
+    return tk::kErrMisaligned;
+  if ((reinterpret_cast<uintptr_t>(lse) & 3u) || (reinterpret_cast<uintptr_t>(delta) & 3u))
+    return tk::kErrMisaligned;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  const int64_t bh = batch * heads;
+  CUtensorMap mq, mk, mv, mdo, mdk, mdv;
+  if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdo, d_o, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdk, dk, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdv, dv, bh, seq, head_dim, dtype)) return rc;
+  tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, lse, delta, dq_accum,
+                bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
+                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
+  return tk::launch_attn_bwd(a);
+}
+
+int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream) {
+  if (dq_accum == nullptr || dq == nullptr || n <= 0 || n % 8 != 0) return tk::kErrInvalidArgument;
+  if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
+  if (!aligned16(dq_accum) || !aligned16(dq)) return tk::kErrMisaligned;
+  tk::DqConvertArgs c{dq_accum, dq, n, dtype == TK_DTYPE_BF16, static_cast<cudaStream_t>(stream)};
+  return tk::launch_attn_dq_convert(c);
+}
+
+int tk_attn_bwd(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                const float* delta, float* dq_accum, void* dq, void* dk, void* dv, int64_t batch,
+                int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                void* stream) {
+  if (dq == nullptr) return tk::kErrInvalidArgument;
+  if (!aligned16(dq)) return tk::kErrMisaligned;
+  if (int rc = tk_attn_bwd_fused(q, k, v, d_o, lse, delta, dq_accum, dk, dv, batch, heads, seq,
+                                 head_dim, dtype, causal, scale, stream))
+    return rc;
+  return tk_attn_dq_convert(dq_accum, dq, batch * heads * seq * head_dim, dtype, stream);
+}
+
+size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim) {
+  if (batch <= 0 || heads <= 0 || seq <= 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(batch) * static_cast<size_t>(heads) * static_cast<size_t>(seq) *
+         static_cast<size_t>(head_dim) * sizeof(float);
+}
+
+int tk_attn_device_status(int* status_out, void* stream) {
+  if (status_out == nullptr) return tk::kErrInvalidArgument;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return tk::kErrLaunch;
+  int value = 0;
+  if (cudaMemcpy(&value, status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return tk::kErrLaunch;
+  const int zero = 0;
+  if (cudaMemcpy(status, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
+    return tk::kErrLaunch;
+  *status_out = value;
+  return tk::kOk;
+}
+
+int tk_attn_set_wait_timeout_ns(unsigned long long timeout_ns) {
+  if (timeout_ns == 0) return tk::kErrInvalidArgument;
+  g_timeout_ns = timeout_ns;
+  return tk::kOk;
+}
+
+int tk_attn_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {
+  if (timeout_ns == 0 || timeout_ns > 10000000000ull) return tk::kErrInvalidArgument;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  return tk::launch_wait_timeout_selftest(timeout_ns, status, static_cast<cudaStream_t>(stream));
+}
+
+int tk_attn_diag_umma(const void* a, const void* b, float* c, int mode, int n, int dtype,
+                      void* stream) {
+  if (a == nullptr || b == nullptr || c == nullptr) return tk::kErrInvalidArgument;
+  if (mode < 0 || mode > 3) return tk::kErrInvalidArgument;
+  if (mode == 0) n = 128;
+  if (n != 64 && n != 128) return tk::kErrUnsupported;
+  if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return tk::kErrMisaligned;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  CUtensorMap ma, mb;
+  if (int rc = make_map(&ma, a, 1, 128, 128, dtype)) return rc;
+  if (int rc = make_map(&mb, b, 1, 128, n, dtype)) return rc;
+  return tk::launch_umma_diag(&ma, &mb, static_cast<const uint32_t*>(a), c, mode, n,
+                              dtype == TK_DTYPE_BF16, g_timeout_ns, status,
+                              static_cast<cudaStream_t>(stream));
+}
+
+const char* tk_attn_status_string(int status) {
+  switch (status & 0xff) {
+    case TK_OK: return "ok";
+    case TK_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case TK_ERR_UNSUPPORTED: return "unsupported dtype or head_dim";
+    case TK_ERR_MISALIGNED: return "misaligned pointer";
+    case TK_ERR_LAUNCH: return "CUDA launch failure";
+    case TK_ERR_TENSOR_MAP: return "TMA tensor map encoding failed";
+    case TK_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    case TK_ERR_NO_DRIVER: return "CUDA driver or device unavailable";
+    case TK_ERR_TOO_LARGE: return "problem size exceeds the supported range";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

@@ -1,0 +1,365 @@
+// Flash-attention forward for sm_100a (B200): TMA-fed Q/K/V tiles, tcgen05
+// MMAs accumulating S = Q.K^T and O += P.V in tensor memory, online softmax
+// in base 2 with the scale folded in, causal tile skipping and a separate
+// masked path for the diagonal / ragged-tail key tile.
+//
+// Semantics follow the reference Triton kernel
+// (src/tklab/kernels/flash_attention.py:54-117 `_attention_inner` and
+// :120-264 `_flash_attention_forward_kernel`): scores are scaled by
+// scale*log2(e) before the running maximum, probabilities are exp2 of the
+// scaled score minus the running maximum, P is rounded to the input dtype
+// for the P.V product, O = acc / row_sum, and the optional statistic is the
+// base-2 log-sum-exp `row_max + log2(row_sum)` (:254-264).
+//
+// One CTA owns one 128-row query tile of one (batch, head).  Warp roles:
+//   warp 0      TMA producer (Q once, then K and V tiles through a ring)
+//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
+//   warps 2..5  softmax: thread t owns query row t (= TMEM lane t), also
+//               rescales O when the running maximum moves, and runs the
+//               epilogue (normalise, stage in smem, TMA store, LSE store).
+// Tensor memory (512 columns): O at [0, D), two S buffers of 128 columns at
+// 128 and 256 so the MMA warp computes S(j+1) while softmax works on S(j).
+// P(j) is written back as packed 16-bit pairs over the first 64 columns of
+// its own S buffer and consumed from TMEM by the P.V MMA.
+#include "attn_launch.h"
+#include "sm100_primitives.cuh"
+
+namespace tk {
+namespace {
+
+template <int D>
+struct FwdCfg {
+  static constexpr int kStages = (D == 64) ? 4 : 2;
+  static constexpr int kTileBytes = kTileRows * D * 2;
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kTileBytes;
+  static constexpr int kVOff = kKOff + kStages * kTileBytes;
+  static constexpr int kBarOff = kVOff + kStages * kTileBytes;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2],
+  // p_ready[2], o_done, o_final
+  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 2;
+  static constexpr int kCtlOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kCtlOff + 64;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColO = 0;
+  // S buffer b (0 or 1) starts at column kColS0 + 128 * b.
+  static constexpr uint32_t kColS0 = 128;
+};
+
+constexpr int kFwdThreads = 192;
+// The running maximum used for P is only moved when the true maximum exceeds
+// it by more than this (base-2 units), so P <= 2^8 and O is rescaled rarely.
+// The result is unchanged mathematically because O and row_sum always share
+// the same reference maximum.
+constexpr float kRescaleThreshold = 8.0f;
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaControl* ctl,
+                                          uint64_t timeout_ns, int* status, int site) {
+  const bool ok = mbar_wait(bar, parity, ctl, timeout_ns, status, site);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int D, bool kBf16, bool kMasked>
+__device__ __forceinline__ void softmax_tile(uint32_t (&s)[4][32], int lim, float scale_log2,
+                                             float& m_run, float& l_run, float& alpha,
+                                             bool& need, uint32_t (&pk)[2][32]) {
+  float mx = -INFINITY;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      float v = __uint_as_float(s[b][c]);
+      if constexpr (kMasked) {
+        if (b * 32 + c >= lim) {
+          v = -INFINITY;
+          s[b][c] = __float_as_uint(v);
+        }
+      }
+      mx = fmaxf(mx, v);
+    }
+  }
+  const float m_new = fmaxf(m_run, mx * scale_log2);
+  need = m_new > m_run + kRescaleThreshold;
+  const float m_use = need ? m_new : m_run;
+  alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_use);
+  const float ms = (m_use == -INFINITY) ? 0.0f : m_use;
+  float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+#pragma unroll
+    for (int c = 0; c < 32; c += 2) {
+      const float p0 = ex2(fmaf(__uint_as_float(s[b][c]), scale_log2, -ms));
+      const float p1 = ex2(fmaf(__uint_as_float(s[b][c + 1]), scale_log2, -ms));
+      sum0 += p0;
+      sum1 += p1;
+      pk[b >> 1][(b & 1) * 16 + (c >> 1)] = pack2<kBf16>(p0, p1);
+    }
+  }
+  l_run = l_run * alpha + (sum0 + sum1);
+  m_run = m_use;
+}
+
+template <int D, bool kBf16>
+__global__ void __launch_bounds__(kFwdThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                    float* __restrict__ lse, int S, int BH, int n_mtiles, int causal,
+                    float scale_log2, unsigned long long timeout_ns, int* status) {
+  using C = FwdCfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023u) {
+    if (threadIdx.x == 0) atomicCAS(status, kOk, kErrMisaligned);
+    return;
+  }
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Heaviest query tiles (largest index under a causal mask) launch first.
+  const int mt = n_mtiles - 1 - static_cast<int>(blockIdx.x) / BH;
+  const int bh = static_cast<int>(blockIdx.x) % BH;
+  const int m0 = mt * kTileRows;
+  const int n_ntiles = (S + kTileRows - 1) / kTileRows;
+  const int n_kv = causal ? min(mt + 1, n_ntiles) : n_ntiles;
+
+  uint8_t* sQ = smem + C::kQOff;
+  uint8_t* sK = smem + C::kKOff;
+  uint8_t* sV = smem + C::kVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + C::kStages;
+  uint64_t* v_full = k_empty + C::kStages;
+  uint64_t* v_empty = v_full + C::kStages;
+  uint64_t* s_full = v_empty + C::kStages;
+  uint64_t* p_ready = s_full + 2;
+  uint64_t* o_done = p_ready + 2;
+  uint64_t* o_final = o_done + 1;
+  CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < C::kStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], 4);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
+    ctl->abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tm_q);
+    tma_prefetch_map(&tm_k);
+    tma_prefetch_map(&tm_v);
+    tma_prefetch_map(&tm_o);
+  }
+  if (warp == 1) tmem_alloc(&ctl->tmem_base, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, C::kTileBytes);
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) tma_load_3d(sQ + b * kBlockBytes, &tm_q, q_full, b * 64, m0, bh);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::kStages;
+        const uint32_t ph = (j / C::kStages) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, ctl, timeout_ns, status, 1)) break;
+        mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+        uint8_t* kdst = sK + st * C::kTileBytes;
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b)
+          tma_load_3d(kdst + b * kBlockBytes, &tm_k, &k_full[st], b * 64, j * kTileRows, bh);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, ctl, timeout_ns, status, 2)) break;
+        mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+        uint8_t* vdst = sV + st * C::kTileBytes;
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b)
+          tma_load_3d(vdst + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc_qk = idesc_f16(kBf16 ? 1u : 0u, 128, 128, 0, 0);
+      const uint32_t idesc_pv = idesc_f16(kBf16 ? 1u : 0u, 128, D, 0, 1);
+      const uint32_t sQa = smem_u32(sQ);
+      const uint32_t sKa = smem_u32(sK);
+      const uint32_t sVa = smem_u32(sV);
+      bool ok = mbar_wait(q_full, 0, ctl, timeout_ns, status, 3);
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
+        const int st = i % C::kStages;
+        if (!mbar_wait(&v_full[st], (i / C::kStages) & 1, ctl, timeout_ns, status, 5)) return false;
+        tc_fence_after();
+        const uint32_t p_col = tmem + C::kColS0 + 128u * (i & 1);
+        const uint32_t v_tile = sVa + st * C::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTileRows / 16; ++kk)
+          umma_ts(tmem + C::kColO, p_col + kk * 8, sdesc_mnmajor(v_tile, kTileRows, kk * 16), idesc_pv,
+                  (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[st]);
+        umma_commit(o_done);
+        return true;
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % C::kStages;
+        if (!mbar_wait(&k_full[st], (j / C::kStages) & 1, ctl, timeout_ns, status, 6)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t s_col = tmem + C::kColS0 + 128u * (j & 1);
+        const uint32_t k_tile = sKa + st * C::kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_ss(s_col, sdesc_kmajor(sQa, kTileRows, kk * 16), sdesc_kmajor(k_tile, kTileRows, kk * 16),
+                  idesc_qk, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[j & 1]);
+        umma_commit(&k_empty[st]);
+        if (j >= 1) ok = issue_pv(j - 1);
+      }
+      if (ok) ok = issue_pv(n_kv - 1);
+      if (ok) umma_commit(o_final);
+    }
+  } else {
+    // ---------------- softmax / correction / epilogue ----------------
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const int row_g = m0 + r;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!warp_wait(&s_full[j & 1], (j >> 1) & 1, ctl, timeout_ns, status, 7)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t s_addr = t_lane + C::kColS0 + 128u * (j & 1);
+      uint32_t s[4][32];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) tmem_ld32(s_addr + b * 32, s[b]);
+      tmem_wait_ld();
+#pragma unroll
+      for (int b = 0; b < 4; ++b) reg_fence(s[b]);
+      const int n0 = j * kTileRows;
+      int lim = S - n0;
+      if (causal) lim = min(lim, row_g - n0 + 1);
+      float alpha;
+      bool need;
+      uint32_t pk[2][32];
+      if (__any_sync(0xffffffffu, lim < kTileRows)) {
+        softmax_tile<D, kBf16, true>(s, lim, scale_log2, m_run, l_run, alpha, need, pk);
+      } else {
+        softmax_tile<D, kBf16, false>(s, lim, scale_log2, m_run, l_run, alpha, need, pk);
+      }
+      tmem_st32(s_addr, pk[0]);
+      tmem_st32(s_addr + 32, pk[1]);
+      if (j >= 1) {
+        // P.V of the previous tile must be finished before O is touched.
+        if (!warp_wait(o_done, (j - 1) & 1, ctl, timeout_ns, status, 8)) {
+          ok = false;
+          break;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          tc_fence_after();
+#pragma unroll
+          for (int cb = 0; cb < D / 32; ++cb) {
+            uint32_t o[32];
+            tmem_ld32(t_lane + C::kColO + cb * 32, o);
+            tmem_wait_ld();
+            reg_fence(o);
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(t_lane + C::kColO + cb * 32, o);
+          }
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_ready[j & 1]);
+    }
+    if (ok) ok = warp_wait(o_final, 0, ctl, timeout_ns, status, 9);
+    if (ok) {
+      tc_fence_after();
+      const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+#pragma unroll
+      for (int cb = 0; cb < D / 32; ++cb) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + C::kColO + cb * 32, o);
+        tmem_wait_ld();
+        reg_fence(o);
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint4 w;
+          w.x = pack2<kBf16>(__uint_as_float(o[ch * 8 + 0]) * inv_l, __uint_as_float(o[ch * 8 + 1]) * inv_l);
+          w.y = pack2<kBf16>(__uint_as_float(o[ch * 8 + 2]) * inv_l, __uint_as_float(o[ch * 8 + 3]) * inv_l);
+          w.z = pack2<kBf16>(__uint_as_float(o[ch * 8 + 4]) * inv_l, __uint_as_float(o[ch * 8 + 5]) * inv_l);
+          w.w = pack2<kBf16>(__uint_as_float(o[ch * 8 + 6]) * inv_l, __uint_as_float(o[ch * 8 + 7]) * inv_l);
+          *reinterpret_cast<uint4*>(sQ + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    // Every softmax warp reaches this barrier exactly once, aborted or not.
+    named_barrier_sync(1, 128);
+    if (warp == 2 && lane == 0 && !ctl->abort) {
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) tma_store_3d(&tm_o, sQ + b * kBlockBytes, b * 64, m0, bh);
+      tma_store_commit();
+      tma_store_wait_read_all();
+    }
+    if (ok && lse != nullptr && row_g < S)
+      lse[static_cast<size_t>(bh) * S + row_g] = m_run + lg2(l_run);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <int D, bool kBf16>
+int launch_fwd_t(const FwdArgs& a) {
+  using C = FwdCfg<D>;
+  auto kern = attn_fwd_kernel<D, kBf16>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
+        cudaSuccess)
+      return kErrLaunch;
+    attr_set[dev] = true;
+  }
+  const int n_mtiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
+  const long long grid = static_cast<long long>(n_mtiles) * a.BH;
+  kern<<<static_cast<unsigned>(grid), kFwdThreads, C::kSmemBytes, a.stream>>>(
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), static_cast<int>(a.BH),
+      n_mtiles, a.causal, a.scale_log2, a.timeout_ns, a.status);
+  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+}
+
+}  // namespace
+
+int launch_attn_fwd(const FwdArgs& a) {
+  if (a.D == 64) return a.bf16 ? launch_fwd_t<64, true>(a) : launch_fwd_t<64, false>(a);
+  if (a.D == 128) return a.bf16 ? launch_fwd_t<128, true>(a) : launch_fwd_t<128, false>(a);
+  return kErrUnsupported;
+}
+
+}  // namespace tk

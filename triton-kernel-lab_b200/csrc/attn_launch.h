@@ -1,0 +1,73 @@
+// Internal launch interface between the C ABI (attn_capi.cu) and the kernel
+// translation units.  Host-only; plain structs, no torch types.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace tk {
+
+struct FwdArgs {
+  const CUtensorMap* tm_q;
+  const CUtensorMap* tm_k;
+  const CUtensorMap* tm_v;
+  const CUtensorMap* tm_o;
+  float* lse;  // nullptr: do not store the statistic
+  int64_t BH, S, D;
+  bool bf16;
+  int causal;
+  float scale_log2;
+  unsigned long long timeout_ns;
+  int* status;
+  cudaStream_t stream;
+};
+
+struct BwdPreArgs {
+  const void* o;
+  const void* d_o;
+  float* delta;
+  float* dq_accum;  // zeroed here; nullptr skips the clear
+  int64_t BH, S, D;
+  bool bf16;
+  cudaStream_t stream;
+};
+
+struct BwdArgs {
+  const CUtensorMap* tm_q;
+  const CUtensorMap* tm_k;
+  const CUtensorMap* tm_v;
+  const CUtensorMap* tm_do;
+  const CUtensorMap* tm_dk;
+  const CUtensorMap* tm_dv;
+  const float* lse;
+  const float* delta;
+  float* dq_accum;
+  int64_t BH, S, D;
+  bool bf16;
+  int causal;
+  float scale;       // softmax scale, applied to dQ and dK
+  float scale_log2;  // scale * log2(e), used to recompute P
+  unsigned long long timeout_ns;
+  int* status;
+  cudaStream_t stream;
+};
+
+struct DqConvertArgs {
+  const float* dq_accum;
+  void* dq;
+  int64_t n;  // elements
+  bool bf16;
+  cudaStream_t stream;
+};
+
+int launch_attn_fwd(const FwdArgs& a);
+int launch_attn_bwd_pre(const BwdPreArgs& a);
+int launch_attn_bwd(const BwdArgs& a);
+int launch_attn_dq_convert(const DqConvertArgs& a);
+int launch_wait_timeout_selftest(unsigned long long timeout_ns, int* status, cudaStream_t stream);
+int launch_umma_diag(const CUtensorMap* tm_a, const CUtensorMap* tm_b, const uint32_t* a_words, float* c,
+                     int mode, int n, bool bf16, unsigned long long timeout_ns, int* status,
+                     cudaStream_t stream);
+
+}  // namespace tk

@@ -1,0 +1,415 @@
+"""Flash attention forward and backward on B200 (sm_100a), behind the
+reference module's interface.
+
+This module keeps every public and test-facing name of the reference's
+``src/tklab/kernels/flash_attention.py`` (``attention_noncausal``,
+``attention_causal``, ``_launch_forward``, ``_launch_backward``,
+``_FlashAttentionFunction``, ``_validate``, the ``ATTENTION_*`` registry
+entries ...) with the same signatures, error messages and launch semantics,
+but the work is done by hand-written CUDA kernels for sm_100a in
+``libtklab_attn.so`` (TMA + tcgen05 + TMEM), reached through its C ABI.
+There is no Triton and no CPU fallback: without the library every call
+raises.
+
+Contract differences from the reference, all widenings:
+* dtypes float16 and bfloat16 (reference: float16 only, ``:281-282``);
+* head_dim 64 or 128 (reference: 64 only, ``:283-284``).
+"""
+
+from __future__ import annotations
+
+import math
+import os
+from typing import Any, cast
+
+import torch
+import torch.nn.functional as F
+from torch.autograd.function import once_differentiable
+
+from tklab import _native
+from tklab.harness.addressing import assert_int32_addressable
+from tklab.harness.tolerances import assert_relative_frobenius
+from tklab.registry import (
+    BenchmarkMetadataFn,
+    BenchmarkScalar,
+    CostFn,
+    KernelSpec,
+    LaunchFn,
+    TensorArgs,
+    TensorFn,
+    register,
+)
+
+# Registered benchmark problem (kept equal to the reference so the FLOP model
+# and result files line up, src/tklab/kernels/flash_attention.py:27-29).
+_BATCH = 1
+_HEADS = 16
+_HEAD_DIM = 64
+
+SUPPORTED_HEAD_DIMS = (64, 128)
+_NATIVE_DTYPE = {torch.float16: _native.TK_DTYPE_F16, torch.bfloat16: _native.TK_DTYPE_BF16}
+
+# Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile,
+# forward CTA = 6 warps, K/V ring depth 4 (head_dim 64) or 2 (head_dim 128).
+_BLOCK_M = 128
+_BLOCK_N = 128
+_FWD_WARPS = 6
+_BWD_WARPS = 10
+
+
+def _fwd_stages(head_dim: int) -> int:
+    return 4 if head_dim == 64 else 2
+
+
+# Set TKLAB_CHECK_DEVICE_STATUS=1 to synchronise after every launch and raise
+# on a device-side error (bounded wait that ran out).  Off by default so
+# launches stay asynchronous like the reference's Triton launches.
+_CHECK_STATUS = os.environ.get("TKLAB_CHECK_DEVICE_STATUS", "0") == "1"
+
+
+def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
+    """Validate the dense self-attention contract (same order as the reference, ``:267-288``)."""
+    if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
+        raise ValueError("attention expects Q, K, and V shaped (batch, heads, sequence, dim)")
+    if q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("Q, K, and V must have identical shapes")
+    if 0 in q.shape:
+        raise ValueError("attention does not support empty dimensions")
+    if q.device != k.device or q.device != v.device:
+        raise ValueError("Q, K, and V must be on the same device")
+    if q.device.type != "cuda":
+        raise ValueError("attention requires CUDA tensors")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise ValueError("Q, K, and V must have the same dtype")
+    if q.dtype not in _NATIVE_DTYPE:
+        raise ValueError("attention currently supports float16 and bfloat16 inputs only")
+    if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
+        raise ValueError(f"attention currently requires head_dim in {SUPPORTED_HEAD_DIMS}")
+    for name, tensor in (("Q", q), ("K", k), ("V", v)):
+        if not tensor.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        assert_int32_addressable(tensor, name=name)
+
+
+def _stream(tensor: torch.Tensor) -> int:
+    return int(torch.cuda.current_stream(tensor.device).cuda_stream)
+
+
+def check_device_status(device: torch.device | int | None = None) -> None:
+    """Synchronise the current stream of ``device`` and raise if a kernel
+    reported a device-side error (a bounded wait that ran out)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        status = _native.device_status(int(torch.cuda.current_stream(dev).cuda_stream))
+    _native.check(status, "attention kernel (device status)")
+
+
+def _after_launch(device: torch.device) -> None:
+    if _CHECK_STATUS:
+        check_device_status(device)
+
+
+def _make_output(args: TensorArgs) -> torch.Tensor:
+    """Allocate the dense attention output."""
+    return torch.empty_like(args[0])
+
+
+def _launch_forward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    output: torch.Tensor,
+    softmax_lse: torch.Tensor,
+    *,
+    causal: bool,
+    store_lse: bool,
+) -> None:
+    """Launch online-softmax attention into preallocated buffers.
+
+    ``softmax_lse`` receives the per-query base-2 log-sum-exp (scale
+    included) when ``store_lse`` is set; otherwise it is an unused
+    placeholder, exactly as in the reference launcher (``:296-347``).
+    """
+    _validate(q, k, v)
+    if output.shape != q.shape or output.device != q.device or output.dtype != q.dtype:
+        raise ValueError("attention output metadata must match Q")
+    if not output.is_contiguous():
+        raise ValueError("attention output must be contiguous")
+    batch, heads, n_ctx, head_dim = q.shape
+    lse_ptr = None
+    if store_lse:
+        if (
+            softmax_lse.shape != (batch, heads, n_ctx)
+            or softmax_lse.device != q.device
+            or softmax_lse.dtype != torch.float32
+            or not softmax_lse.is_contiguous()
+        ):
+            raise ValueError("attention log-sum-exp buffer must be contiguous float32 BxHxN")
+        assert_int32_addressable(softmax_lse, name="log-sum-exp buffer")
+        lse_ptr = softmax_lse.data_ptr()
+    lib = _native.load()
+    with torch.cuda.device(q.device):
+        status = lib.tk_attn_fwd(
+            q.data_ptr(),
+            k.data_ptr(),
+            v.data_ptr(),
+            output.data_ptr(),
+            lse_ptr,
+            batch,
+            heads,
+            n_ctx,
+            head_dim,
+            _NATIVE_DTYPE[q.dtype],
+            int(bool(causal)),
+            1.0 / math.sqrt(head_dim),
+            _stream(q),
+        )
+    _native.check(status, "tk_attn_fwd")
+    _after_launch(q.device)
+
+
+def _launch_factory(*, causal: bool) -> LaunchFn:
+    """Create an allocation-free, inference-only launcher for one masking mode."""
+
+    def launch(args: TensorArgs, output: torch.Tensor) -> None:
+        """Launch forward attention without saving backward statistics."""
+        q, k, v = args
+        _launch_forward(q, k, v, output, output, causal=causal, store_lse=False)
+
+    return launch
+
+
+_launch_noncausal = _launch_factory(causal=False)
+_launch_causal = _launch_factory(causal=True)
+
+
+def _launch_backward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    output: torch.Tensor,
+    softmax_lse: torch.Tensor,
+    do: torch.Tensor,
+    *,
+    causal: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Run the recompute backward and return ``(dQ, dK, dV)`` (reference ``:536-607``).
+
+    Two library calls: ``tk_attn_bwd_pre`` (delta = rowsum(dO * O) and a
+    cleared fp32 dQ accumulator) and ``tk_attn_bwd`` (the fused tcgen05
+    kernel for dK, dV and dQ, then the dQ conversion).
+    """
+    if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
+        raise ValueError("attention upstream gradient metadata must match Q")
+    _validate(q, k, v)
+    do = do.contiguous()
+    batch, heads, n_ctx, head_dim = q.shape
+    if (
+        softmax_lse.shape != (batch, heads, n_ctx)
+        or softmax_lse.dtype != torch.float32
+        or not softmax_lse.is_contiguous()
+    ):
+        raise ValueError("attention log-sum-exp buffer must be contiguous float32 BxHxN")
+    delta = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
+    dq_accum = torch.empty((batch, heads, n_ctx, head_dim), dtype=torch.float32, device=q.device)
+    dq = torch.empty_like(q)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    lib = _native.load()
+    dtype = _NATIVE_DTYPE[q.dtype]
+    with torch.cuda.device(q.device):
+        stream = _stream(q)
+        status = lib.tk_attn_bwd_pre(
+            output.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+            batch, heads, n_ctx, head_dim, dtype, stream,
+        )
+        _native.check(status, "tk_attn_bwd_pre")
+        status = lib.tk_attn_bwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+            softmax_lse.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+            dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+            batch, heads, n_ctx, head_dim, dtype, int(bool(causal)),
+            1.0 / math.sqrt(head_dim), stream,
+        )
+        _native.check(status, "tk_attn_bwd")
+    _after_launch(q.device)
+    return dq, dk, dv
+
+
+class _FlashAttentionFunction(torch.autograd.Function):
+    """Autograd bridge: forward saves Q/K/V, O and the base-2 LSE; backward recomputes P."""
+
+    @staticmethod
+    def forward(
+        ctx: Any,
+        q: torch.Tensor,
+        k: torch.Tensor,
+        v: torch.Tensor,
+        causal: bool,
+    ) -> torch.Tensor:
+        """Run the forward kernel with the statistic stored for the backward."""
+        _validate(q, k, v)
+        output = torch.empty_like(q)
+        batch, heads, n_ctx, _ = q.shape
+        softmax_lse = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
+        _launch_forward(q, k, v, output, softmax_lse, causal=causal, store_lse=True)
+        ctx.save_for_backward(q, k, v, output, softmax_lse)
+        ctx.causal = causal
+        return output
+
+    @staticmethod
+    @once_differentiable
+    def backward(
+        ctx: Any,
+        do: torch.Tensor,
+    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, None]:
+        """Compute Q, K and V gradients with the recompute backward."""
+        q, k, v, output, softmax_lse = ctx.saved_tensors
+        dq, dk, dv = _launch_backward(q, k, v, output, softmax_lse, do, causal=ctx.causal)
+        return dq, dk, dv, None
+
+
+def _attention(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool,
+) -> torch.Tensor:
+    """Inference without saved statistics; training through autograd (reference ``:663-686``)."""
+    _validate(q, k, v)
+    needs_grad = torch.is_grad_enabled() and any(tensor.requires_grad for tensor in (q, k, v))
+    if not needs_grad:
+        output = torch.empty_like(q)
+        _launch_forward(q, k, v, output, output, causal=causal, store_lse=False)
+        return output
+    result = _FlashAttentionFunction.apply(q, k, v, causal)
+    return cast(torch.Tensor, result)
+
+
+def attention_noncausal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Compute dense non-causal scaled dot-product attention with autograd."""
+    return _attention(q, k, v, causal=False)
+
+
+def attention_causal(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """Compute dense causal scaled dot-product attention with autograd."""
+    return _attention(q, k, v, causal=True)
+
+
+def _reference_factory(*, causal: bool) -> TensorFn:
+    """PyTorch SDPA reference for one masking mode (reference ``:699-706``)."""
+
+    def reference(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        """Call PyTorch scaled-dot-product attention."""
+        return F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+
+    return reference
+
+
+_reference_noncausal = _reference_factory(causal=False)
+_reference_causal = _reference_factory(causal=True)
+
+
+def _make_inputs(
+    sequence_length: int,
+    device: torch.device,
+    dtype: torch.dtype,
+) -> TensorArgs:
+    """Create contiguous self-attention inputs of the registered shape."""
+    shape = (_BATCH, _HEADS, sequence_length, _HEAD_DIM)
+    return (
+        torch.randn(shape, device=device, dtype=dtype),
+        torch.randn(shape, device=device, dtype=dtype),
+        torch.randn(shape, device=device, dtype=dtype),
+    )
+
+
+def _make_adversarial(device: torch.device) -> TensorArgs:
+    """A sequence length that is not a tile multiple: partial query and key tiles."""
+    return _make_inputs(1000, device, torch.float16)
+
+
+def _assert_attention(output: torch.Tensor, reference: torch.Tensor) -> None:
+    """Validate attention through aggregate FP32-relative error."""
+    assert_relative_frobenius(output, reference, max_relative_error=2e-2)
+
+
+def attention_pairs(sequence_length: int, *, causal: bool) -> int:
+    """Attended (query, key) pairs: S^2, or S(S+1)/2 under the causal mask."""
+    return sequence_length * (sequence_length + 1) // 2 if causal else sequence_length**2
+
+
+def _flops_factory(*, causal: bool) -> CostFn:
+    """Two-matmul forward FLOP model of the reference (``:737-747``)."""
+
+    def flops(sequence_length: int, _dtype: torch.dtype) -> int:
+        """Count QK-transpose and probability-value multiply-adds."""
+        return 4 * _BATCH * _HEADS * attention_pairs(sequence_length, causal=causal) * _HEAD_DIM
+
+    return flops
+
+
+def _metadata_factory(*, causal: bool) -> BenchmarkMetadataFn:
+    """Tile configuration of the sm_100a forward kernel, with the reference's keys (``:750-766``)."""
+
+    def metadata(_size: int, _dtype: torch.dtype) -> dict[str, BenchmarkScalar]:
+        """Return the fixed tile shape and problem dimensions."""
+        return {
+            "block_m": _BLOCK_M,
+            "block_n": _BLOCK_N,
+            "num_warps": _FWD_WARPS,
+            "num_stages": _fwd_stages(_HEAD_DIM),
+            "heads": _HEADS,
+            "head_dim": _HEAD_DIM,
+            "causal": causal,
+        }
+
+    return metadata
+
+
+_SIZES = (512, 1024, 2048, 4096, 8192)
+
+ATTENTION_NONCAUSAL = register(
+    KernelSpec(
+        name="attention_noncausal",
+        description="Flash Attention forward (sm_100a tcgen05) with online softmax and no mask.",
+        triton_fn=attention_noncausal,
+        launch_fn=_launch_noncausal,
+        ref_fn=_reference_noncausal,
+        make_inputs=_make_inputs,
+        make_output=_make_output,
+        make_adversarial=_make_adversarial,
+        sizes=_SIZES,
+        correctness_sizes=(128, 512),
+        bound="compute",
+        flops=_flops_factory(causal=False),
+        dtypes=(torch.float16, torch.bfloat16),
+        assert_fn=_assert_attention,
+        benchmark_metadata=_metadata_factory(causal=False),
+        compute_mode="attention_fp16_fp32acc",
+        supports_interpreter=False,
+    )
+)
+
+ATTENTION_CAUSAL = register(
+    KernelSpec(
+        name="attention_causal",
+        description="Flash Attention forward (sm_100a tcgen05) with causal tile skipping.",
+        triton_fn=attention_causal,
+        launch_fn=_launch_causal,
+        ref_fn=_reference_causal,
+        make_inputs=_make_inputs,
+        make_output=_make_output,
+        make_adversarial=_make_adversarial,
+        sizes=_SIZES,
+        correctness_sizes=(128, 512),
+        bound="compute",
+        flops=_flops_factory(causal=True),
+        dtypes=(torch.float16, torch.bfloat16),
+        assert_fn=_assert_attention,
+        benchmark_metadata=_metadata_factory(causal=True),
+        compute_mode="attention_fp16_fp32acc",
+        supports_interpreter=False,
+    )
+)
