@@ -72,35 +72,44 @@ def bwd_flops(b: int, h: int, s: int, d: int, causal: bool) -> int:
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons in the background during the timed region."""
+    """Streams ``nvidia-smi -lms 100`` clock / throttle-reason samples while active."""
 
     def __init__(self, index: int) -> None:
         self.index = index
         self.samples: list[tuple[float, float, int]] = []
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._proc: subprocess.Popen | None = None
+        self._thread = threading.Thread(target=self._read, daemon=True)
 
-    def _run(self) -> None:
-        query = "clocks.sm,clocks.max.sm,clocks_event_reasons.active"
-        while not self._stop.is_set():
+    def _read(self) -> None:
+        assert self._proc is not None and self._proc.stdout is not None
+        for line in self._proc.stdout:
             try:
-                out = subprocess.run(
-                    ["nvidia-smi", "-i", str(self.index), f"--query-gpu={query}", "--format=csv,noheader,nounits"],
-                    capture_output=True, text=True, timeout=5, check=False,
-                ).stdout.strip()
-                sm, sm_max, reasons = (x.strip() for x in out.split(","))
+                sm, sm_max, reasons = (x.strip() for x in line.split(","))
                 self.samples.append((float(sm), float(sm_max), int(reasons, 16)))
-            except Exception:  # noqa: BLE001 - sampling is best-effort
-                pass
-            self._stop.wait(0.2)
+            except ValueError:
+                continue
 
     def __enter__(self) -> ClockSampler:
-        self._thread.start()
+        query = "clocks.sm,clocks.max.sm,clocks_event_reasons.active"
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={query}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            self._thread.start()
+        except OSError:
+            self._proc = None
         return self
 
     def __exit__(self, *exc: object) -> None:
-        self._stop.set()
-        self._thread.join(timeout=10)
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._thread.join(timeout=5)
 
     def summary(self) -> dict:
         if not self.samples:
@@ -144,11 +153,12 @@ def run_ours(args: argparse.Namespace) -> None:
 
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=device)
+    from tklab.sharding import slab_range
+
     b, h, s, d, dtype, causal, qk_std = CONFIGS[args.config]
     bh_total = b * h
-    if bh_total % world:
-        raise SystemExit(f"{bh_total} (batch*head) slabs do not split over {world} ranks")
-    slab = bh_total // world
+    start_bh, stop_bh = slab_range(bh_total, world, rank)
+    slab = stop_bh - start_bh
     shape = (1, slab, s, d)  # this rank's contiguous slab of the flattened (B*H) axis
     lib = _native.load()
     q, k, v, do = _make_inputs(shape, dtype, qk_std, seed=args.seed + rank, device=device)
@@ -418,7 +428,7 @@ def run_reference(args: argparse.Namespace) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--steps", type=int, default=30)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--config", choices=tuple(CONFIGS), default="c3")
