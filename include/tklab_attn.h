@@ -93,6 +93,23 @@ TK_API int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const 
                              int dtype, int causal, float scale, void* stream);
 TK_API int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream);
 
+/* The backward for callers that cannot allocate device memory (code inside a
+ * fixed-memory graph capture, frameworks that own every device byte through
+ * their own pool, allocation-free hot loops).  Same inputs and outputs as
+ * tk_attn_bwd_pre + tk_attn_bwd, but delta and the fp32 dQ accumulator live
+ * in a 64 MiB array compiled into the library instead of caller buffers, so
+ * nothing is allocated.  Limit: batch*heads*seq*(head_dim+1) <= 16,777,216,
+ * else TK_ERR_TOO_LARGE before any launch.  The array is shared by all calls
+ * on a device: calls whose kernels overlap on the GPU race on it; each call
+ * clears the accumulator it needs.  The first call on a device looks up the
+ * array's device address — make it before any stream capture.  Every GPU
+ * that loads this part of the library holds the 64 MiB until exit.
+ * No counterpart in the reference (its backward allocates through torch). */
+TK_API int tk_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
+                               const void* d_o, const float* lse, void* dq, void* dk, void* dv,
+                               int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                               int dtype, int causal, float scale, void* stream);
+
 /* Bytes of the fp32 dQ accumulator tk_attn_bwd needs (0 on bad sizes). */
 TK_API size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);
 
