@@ -157,6 +157,9 @@ def run_ours(args: argparse.Namespace) -> None:
 
     b, h, s, d, dtype, causal, qk_std = CONFIGS[args.config]
     bh_total = b * h
+    if args.bh is not None:
+        # Profiling mode: a smaller problem of the same per-slab shape.
+        bh_total = args.bh * world
     start_bh, stop_bh = slab_range(bh_total, world, rank)
     slab = stop_bh - start_bh
     shape = (1, slab, s, d)  # this rank's contiguous slab of the flattened (B*H) axis
@@ -246,8 +249,8 @@ def run_ours(args: argparse.Namespace) -> None:
     if rank == 0:
         peaks = _peaks()
         steps = args.steps
-        ff = fwd_flops(b, h, s, d, causal)
-        bf = bwd_flops(b, h, s, d, causal)
+        ff = fwd_flops(1, bh_total, s, d, causal)
+        bf = bwd_flops(1, bh_total, s, d, causal)
         ms_per_step = total_ms / steps
         value = (ff + bf) / (ms_per_step * 1e-3) / 1e12
         # Dominant kernel: the one with the largest share of the step.
@@ -276,6 +279,7 @@ def run_ours(args: argparse.Namespace) -> None:
                 "heads": h,
                 "head_dim": d,
                 "parallelism": f"(batch*head) slabs {slab}/rank x {world} ranks, no collective",
+                "bh_total": bh_total,
                 "l2": "flushed: 256 MiB write before every timed step (outside its events)",
             },
             "fwd_tflops_per_gpu": round(ff / world / (k_fwd / steps * 1e-3) / 1e12, 2),
@@ -437,6 +441,8 @@ def main() -> None:
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--bh", type=int, default=None,
+                        help="(batch*head) slabs per rank instead of the config's (profiling only)")
     parser.add_argument("--traffic-bytes", type=float, default=None,
                         help="ncu dram bytes per launch of the dominant kernel, if captured")
     args = parser.parse_args()
