@@ -47,8 +47,8 @@ struct BwdCfg {
   static constexpr int kDeltaOff = kLseOff + 2 * 128 * 4;  // float[2][128]
   static constexpr int kBarOff = kDeltaOff + 2 * 128 * 4;
   // kv_full, q_full[QS], do_full[QS], qdo_empty[QS], ld_full[2], ld_empty[2],
-  // s_full, dp_full, ds_ready, ds_empty, dq_full, dq_empty, dkdv_done
-  static constexpr int kNumBars = 1 + 3 * kQStages + 4 + 7;
+  // s_full, dp_full, p_ready, ds_ready, ds_empty, dq_full, dq_empty, dkdv_done
+  static constexpr int kNumBars = 1 + 3 * kQStages + 4 + 8;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -58,6 +58,11 @@ struct BwdCfg {
   static constexpr uint32_t kColDP = 2 * D + 128;
   static constexpr bool kDqAliased = (2 * D + 256 + D) > 512;
   static constexpr uint32_t kColDQ = kDqAliased ? kColDP : 2 * D + 256;
+  // head_dim 128: dQ is produced transposed (M = head_dim, N = queries) so a
+  // warp's reduction instruction covers one contiguous 128-byte row segment
+  // of the accumulator.  head_dim 64 keeps M = queries (an M = 64 MMA would
+  // use the half-lane TMEM layout).
+  static constexpr bool kDqTransposed = (D == 128);
 };
 
 constexpr int kBwdThreads = 320;
@@ -106,10 +111,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Key tiles with the most query steps (smallest index under a causal mask)
-  // launch first.
-  const int jn = static_cast<int>(blockIdx.x) / BH;
-  const int bh = static_cast<int>(blockIdx.x) % BH;
+  // Head-major order: the key tiles of one (batch, head) are adjacent in the
+  // grid, so resident CTAs share a few heads' Q, dO and dQ-accumulator lines
+  // in L2.  Within a head the key tiles with the most query steps (smallest
+  // index under a causal mask) launch first.
+  const int bh = static_cast<int>(blockIdx.x) / n_tiles;
+  const int jn = static_cast<int>(blockIdx.x) % n_tiles;
   const int n0 = jn * kTileRows;
   const int i_start = causal ? jn : 0;
   const int n_steps = n_tiles - i_start;
@@ -130,7 +137,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* ld_empty = ld_full + 2;
   uint64_t* s_full = ld_empty + 2;
   uint64_t* dp_full = s_full + 1;
-  uint64_t* ds_ready = dp_full + 1;
+  uint64_t* p_ready = dp_full + 1;
+  uint64_t* ds_ready = p_ready + 1;
   uint64_t* ds_empty = ds_ready + 1;
   uint64_t* dq_full = ds_empty + 1;
   uint64_t* dq_empty = dq_full + 1;
@@ -150,6 +158,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
+    mbar_init(p_ready, 4);
     mbar_init(ds_ready, 4);
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
@@ -214,61 +223,81 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
+    // Order per step i:  dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}.  S_{i+1} goes
+    // out as soon as dV_i has consumed P_i from the S columns, so the dS
+    // warps compute P_{i+1} (the exp2-heavy half of their work) while the
+    // tensor core runs dK_i and dQ_i.
     if (lane == 0) {
       const uint32_t fmt = kBf16 ? 1u : 0u;
       const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
       const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
-      const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
+      const uint32_t idesc_dq = C::kDqTransposed ? idesc_f16(fmt, D, 128, 1, 1) : idesc_f16(fmt, 128, D, 1, 1);
       const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sDSa = smem_u32(sDS);
-      bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 3);
-      for (int it = 0; ok && it < n_steps; ++it) {
+      auto issue_s = [&](int it) -> bool {
         const int st = it % C::kQStages;
-        const uint32_t ph = (it / C::kQStages) & 1;
-        const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
-        const uint32_t sDOa = smem_u32(sDO + st * C::kTileBytes);
-        // S^T = K Q^T
-        if (!(ok = mbar_wait(&q_full[st], ph, ctl, timeout_ns, status, 4))) break;
+        if (!mbar_wait(&q_full[st], (it / C::kQStages) & 1, ctl, timeout_ns, status, 4)) return false;
         tc_fence_after();
+        const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_ss(tmem + C::kColS, sdesc_kmajor(sKa, kTileRows, kk * 16),
                   sdesc_kmajor(sQa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(s_full);
-        // dP^T = V dO^T
-        if (!(ok = mbar_wait(&do_full[st], ph, ctl, timeout_ns, status, 5))) break;
+        return true;
+      };
+      auto issue_dp = [&](int it) -> bool {
+        const int st = it % C::kQStages;
+        if (!mbar_wait(&do_full[st], (it / C::kQStages) & 1, ctl, timeout_ns, status, 5)) return false;
         if (C::kDqAliased && it > 0) {
-          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6))) break;
+          if (!mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
         }
         tc_fence_after();
+        const uint32_t sDOa = smem_u32(sDO + st * C::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_ss(tmem + C::kColDP, sdesc_kmajor(sVa, kTileRows, kk * 16),
                   sdesc_kmajor(sDOa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(dp_full);
-        // P^T (TMEM) and dS^T (smem) from the dS warps
-        if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 7))) break;
+        return true;
+      };
+      bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 3);
+      if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
+      for (int it = 0; ok && it < n_steps; ++it) {
+        const int st = it % C::kQStages;
+        const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
+        const uint32_t sDOa = smem_u32(sDO + st * C::kTileBytes);
+        // dV += P^T dO  (P^T packed in the S columns by the dS warps)
+        if (!(ok = mbar_wait(p_ready, it & 1, ctl, timeout_ns, status, 7))) break;
         tc_fence_after();
-        // dV += P^T dO
 #pragma unroll
         for (int kk = 0; kk < kTileRows / 16; ++kk)
           umma_ts(tmem + C::kColDV, tmem + C::kColS + kk * 8, sdesc_mnmajor(sDOa, kTileRows, kk * 16),
                   idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-        // dK += dS^T Q
+        if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
+        // dK += dS^T Q  (dS^T in smem from the dS warps)
+        if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 8))) break;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTileRows / 16; ++kk)
           umma_ss(tmem + C::kColDK, sdesc_kmajor(sDSa, kTileRows, kk * 16),
                   sdesc_mnmajor(sQa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&qdo_empty[st]);
-        // dQ = dS K
+        // dQ = dS K, or dQ^T = K^T dS^T (head_dim 128)
         if (!C::kDqAliased && it > 0) {
-          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 8))) break;
+          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 9))) break;
         }
 #pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk)
-          umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
-                  sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < kTileRows / 16; ++kk) {
+          if constexpr (C::kDqTransposed)
+            umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sKa, kTileRows, kk * 16),
+                    sdesc_mnmajor(sDSa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
+          else
+            umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
+                    sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
+        }
         umma_commit(dq_full);
         umma_commit(ds_empty);
+        if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
       }
       if (ok) umma_commit(dkdv_done);
     }
@@ -282,44 +311,58 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int it = 0; it < n_steps; ++it) {
       const int i = i_start + it;
       const int lb = it & 1;
-      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 9))) break;
-      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 10))) break;
-      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 11))) break;
-      if (it > 0) {
-        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 12))) break;
-      }
+      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 10))) break;
+      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 11))) break;
       tc_fence_after();
       const bool diag = causal && (i == jn);
       const float* lse_s = sLse + lb * 128;
       const float* del_s = sDelta + lb * 128;
+      // Phase 1: P^T row (all 128 queries of the step) -> registers and,
+      // packed to 16 bits, back over the S columns for the dV MMA.
+      float p[4][32];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], dpv[32];
+        uint32_t sv[32];
         tmem_ld32(t_lane + C::kColS + c * 32, sv);
-        tmem_ld32(t_lane + C::kColDP + c * 32, dpv);
         tmem_wait_ld();
         reg_fence(sv);
+        uint32_t pp[16];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int q = c * 32 + e;
+          float pv = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse_s[q]));
+          if (diag && q < t) pv = 0.0f;
+          if (!key_ok) pv = 0.0f;
+          p[c][e] = pv;
+        }
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
+        tmem_st16(t_lane + C::kColS + c * 16, pp);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // Phase 2: dS^T = P^T (dP^T - delta) -> smem for the dK and dQ MMAs.
+      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 12))) break;
+      if (it > 0) {
+        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 13))) break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t dpv[32];
+        tmem_ld32(t_lane + C::kColDP + c * 32, dpv);
+        tmem_wait_ld();
         reg_fence(dpv);
-        uint32_t pp[16], dd[16];
+        uint32_t dd[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int q = c * 32 + e;
-          float p0 = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse_s[q]));
-          float p1 = ex2(fmaf(__uint_as_float(sv[e + 1]), scale_log2, -lse_s[q + 1]));
-          if (diag) {
-            if (q < t) p0 = 0.0f;
-            if (q + 1 < t) p1 = 0.0f;
-          }
-          if (!key_ok) {
-            p0 = 0.0f;
-            p1 = 0.0f;
-          }
-          const float d0 = p0 * (__uint_as_float(dpv[e]) - del_s[q]);
-          const float d1 = p1 * (__uint_as_float(dpv[e + 1]) - del_s[q + 1]);
-          pp[e >> 1] = pack2<kBf16>(p0, p1);
+          const float d0 = p[c][e] * (__uint_as_float(dpv[e]) - del_s[q]);
+          const float d1 = p[c][e + 1] * (__uint_as_float(dpv[e + 1]) - del_s[q + 1]);
           dd[e >> 1] = pack2<kBf16>(d0, d1);
         }
-        tmem_st16(t_lane + C::kColS + c * 16, pp);
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           uint4 v = make_uint4(dd[w * 4 + 0], dd[w * 4 + 1], dd[w * 4 + 2], dd[w * 4 + 3]);
@@ -327,7 +370,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
       }
       fence_proxy_async_smem();
-      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -351,35 +393,62 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_store_wait_read_all();
     }
   } else {
-    // ---------------- dQ warps: thread r owns query m0 + r ----------------
+    // ---------------- dQ warps ----------------
+    // head_dim 128: thread r owns head-dim column r of dQ^T and, for every
+    // query m of the step, the 32 lanes of a warp add 32 consecutive floats
+    // (one 128-byte segment of row m).  head_dim 64: thread r owns query
+    // m0 + r and adds its row with 16-byte vector atomics.
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
     bool ok = true;
     for (int it = 0; it < n_steps; ++it) {
-      const int mg = (i_start + it) * kTileRows + r;
+      const int m0 = (i_start + it) * kTileRows;
       if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 14))) break;
       tc_fence_after();
-      uint32_t v[D / 32][32];
+      if constexpr (C::kDqTransposed) {
+        uint32_t v[4][32];
 #pragma unroll
-      for (int cb = 0; cb < D / 32; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
-      tmem_wait_ld();
+        for (int cb = 0; cb < 4; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
+        tmem_wait_ld();
 #pragma unroll
-      for (int cb = 0; cb < D / 32; ++cb) reg_fence(v[cb]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      if (mg < S) {
-        float4* dst = reinterpret_cast<float4*>(dq_accum + (row_base + mg) * D);
+        for (int cb = 0; cb < 4; ++cb) reg_fence(v[cb]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        float* col = dq_accum + (row_base + m0) * D + r;
+        const int rows = min(kTileRows, S - m0);
 #pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) {
+        for (int cb = 0; cb < 4; ++cb) {
 #pragma unroll
-          for (int f = 0; f < 8; ++f) {
-            const float4 add = make_float4(__uint_as_float(v[cb][4 * f + 0]) * scale,
-                                           __uint_as_float(v[cb][4 * f + 1]) * scale,
-                                           __uint_as_float(v[cb][4 * f + 2]) * scale,
-                                           __uint_as_float(v[cb][4 * f + 3]) * scale);
-            atomicAdd(dst + cb * 8 + f, add);
+          for (int e = 0; e < 32; ++e) {
+            const int m = cb * 32 + e;
+            if (m < rows) atomicAdd(col + static_cast<size_t>(m) * D, __uint_as_float(v[cb][e]) * scale);
+          }
+        }
+      } else {
+        const int mg = m0 + r;
+        uint32_t v[D / 32][32];
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) reg_fence(v[cb]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+        if (mg < S) {
+          float4* dst = reinterpret_cast<float4*>(dq_accum + (row_base + mg) * D);
+#pragma unroll
+          for (int cb = 0; cb < D / 32; ++cb) {
+#pragma unroll
+            for (int f = 0; f < 8; ++f) {
+              const float4 add = make_float4(__uint_as_float(v[cb][4 * f + 0]) * scale,
+                                             __uint_as_float(v[cb][4 * f + 1]) * scale,
+                                             __uint_as_float(v[cb][4 * f + 2]) * scale,
+                                             __uint_as_float(v[cb][4 * f + 3]) * scale);
+              atomicAdd(dst + cb * 8 + f, add);
+            }
           }
         }
       }

@@ -113,9 +113,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Heaviest query tiles (largest index under a causal mask) launch first.
-  const int mt = n_mtiles - 1 - static_cast<int>(blockIdx.x) / BH;
-  const int bh = static_cast<int>(blockIdx.x) % BH;
+  // Head-major order: the query tiles of one (batch, head) are adjacent in
+  // the grid, so the CTAs resident at any time share a few heads' K/V in L2.
+  // Within a head the heaviest tiles (largest index under a causal mask)
+  // launch first.
+  const int bh = static_cast<int>(blockIdx.x) / n_mtiles;
+  const int mt = n_mtiles - 1 - static_cast<int>(blockIdx.x) % n_mtiles;
   const int m0 = mt * kTileRows;
   const int n_ntiles = (S + kTileRows - 1) / kTileRows;
   const int n_kv = causal ? min(mt + 1, n_ntiles) : n_ntiles;
