@@ -1,6 +1,7 @@
 // Flash-attention backward for sm_100a (B200): one fused recompute kernel that
-// produces dK and dV for a 128-key tile and streams dQ contributions into an
-// fp32 accumulator, all five contractions on tcgen05 with TMEM accumulators.
+// produces dK and dV for a 128-key tile and reduces its dQ contributions into
+// an fp32 accumulator, all five contractions on tcgen05 with TMEM
+// accumulators.
 //
 // Semantics follow the reference kernels `_attn_bwd_dkdv_kernel` and
 // `_attn_bwd_dq_kernel` (src/tklab/kernels/flash_attention.py:398-533):
@@ -11,22 +12,27 @@
 // causal blocks below the diagonal skipped (:438, :513) and the diagonal and
 // ragged tails masked (:454-457, :523-526).  The reference runs dK/dV and dQ
 // as two kernels that both recompute P (14 N^2 d MMA flops); here dQ is
-// produced by the same CTA (10 N^2 d) and reduced across key tiles with
-// 128-bit fp32 atomics.
+// produced by the same CTA (10 N^2 d) and reduced across key tiles by the
+// TMA unit (bulk tensor reduce-add from shared memory).
 //
 // One CTA owns a 128-key tile (K, V resident in smem) of one (batch, head)
 // and walks 128-query steps.  The transposed products are computed directly
 // (S^T = K Q^T, dP^T = V dO^T) so TMEM lane n holds key n:
-//   warp 0      producer: TMA for K, V, Q_i, dO_i; plain loads of LSE/delta
+//   warp 0      producer: TMA for K, V, Q_i (2 stages), dO_i (1 stage);
+//               plain loads of LSE/delta
 //   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 2..5  "dS warps": thread n owns key n; P^T and dS^T for all 128
-//               queries of a step (P^T back to TMEM for the dV MMA, dS^T to
-//               smem for the dK and dQ MMAs); dV epilogue
-//   warps 6..9  "dQ warps": thread m owns query m of the step; read dQ from
-//               TMEM and add it into the fp32 accumulator; dK epilogue
-// TMEM columns: dV [0,D) dK [D,2D) S^T/P^T [2D,2D+128) dP^T [2D+128,2D+256)
-// dQ after dP^T when it fits (D=64), otherwise aliased onto dP^T (D=128),
-// which the next step's dP^T MMA reclaims only once dQ has been read out.
+//   warps 2..5  "dS warps": thread n owns key n.  Phase 1: P^T for the 128
+//               queries of a step, written back as 16-bit over the S^T
+//               columns for the dV MMA.  Phase 2: dS^T = P^T (dP^T - delta)
+//               to smem for the dK and dQ MMAs.  dV epilogue.
+//   warps 6..9  "dQ warps": thread m owns query m of the step; copy dQ from
+//               TMEM into an fp32 staging tile (32 KB, 128-byte swizzle);
+//               warp 6 lane 0 issues the TMA reduce-add.  dK epilogue.
+// MMA issue order per step i: dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}, so the dS
+// warps compute P_{i+1} (the exp2-heavy phase) while dK_i and dQ_i run.
+// TMEM columns: dV [0,D) dK [D,2D) S^T/P^T [2D,2D+128) dP^T [2D+128,2D+256);
+// dQ follows dP^T when it fits (D=64) and otherwise (D=128) reuses the dP^T
+// columns, reclaimed by dP_{i+1} only after the dQ warps have read dQ_i.
 #include "attn_launch.h"
 #include "sm100_primitives.cuh"
 
@@ -35,20 +41,22 @@ namespace {
 
 template <int D>
 struct BwdCfg {
-  static constexpr int kQStages = 2;
   static constexpr int kTileBytes = kTileRows * D * 2;
   static constexpr int kKOff = 0;
   static constexpr int kVOff = kKOff + kTileBytes;
-  static constexpr int kQOff = kVOff + kTileBytes;
-  static constexpr int kDOOff = kQOff + kQStages * kTileBytes;
-  static constexpr int kDSOff = kDOOff + kQStages * kTileBytes;
+  static constexpr int kQOff = kVOff + kTileBytes;  // 2 stages
+  static constexpr int kDOOff = kQOff + 2 * kTileBytes;
+  static constexpr int kDSOff = kDOOff + kTileBytes;
   static constexpr int kDSBytes = kTileRows * kTileRows * 2;
-  static constexpr int kLseOff = kDSOff + kDSBytes;        // float[2][128]
+  static constexpr int kDQOff = kDSOff + kDSBytes;  // fp32 staging: 2 boxes of 128 x 32
+  static constexpr int kDQBytes = 2 * kTileRows * kSwizzleBytes;
+  static constexpr int kLseOff = kDQOff + kDQBytes;        // float[2][128]
   static constexpr int kDeltaOff = kLseOff + 2 * 128 * 4;  // float[2][128]
   static constexpr int kBarOff = kDeltaOff + 2 * 128 * 4;
-  // kv_full, q_full[QS], do_full[QS], qdo_empty[QS], ld_full[2], ld_empty[2],
-  // s_full, dp_full, p_ready, ds_ready, ds_empty, dq_full, dq_empty, dkdv_done
-  static constexpr int kNumBars = 1 + 3 * kQStages + 4 + 8;
+  // kv_full, q_full[2], q_empty[2], do_full, do_empty, ld_full[2], ld_empty[2],
+  // s_full, dp_full, p_ready, ds_ready, ds_empty, dq_full, dq_empty,
+  // stage_full, stage_free, dkdv_done
+  static constexpr int kNumBars = 1 + 4 + 2 + 4 + 10;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -58,11 +66,8 @@ struct BwdCfg {
   static constexpr uint32_t kColDP = 2 * D + 128;
   static constexpr bool kDqAliased = (2 * D + 256 + D) > 512;
   static constexpr uint32_t kColDQ = kDqAliased ? kColDP : 2 * D + 256;
-  // head_dim 128: dQ is produced transposed (M = head_dim, N = queries) so a
-  // warp's reduction instruction covers one contiguous 128-byte row segment
-  // of the accumulator.  head_dim 64 keeps M = queries (an M = 64 MMA would
-  // use the half-lane TMEM layout).
-  static constexpr bool kDqTransposed = (D == 128);
+  // dQ is reduced in passes of 64 head-dim columns (two 32-float boxes).
+  static constexpr int kDqPasses = D / 64;
 };
 
 constexpr int kBwdThreads = 320;
@@ -100,8 +105,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
-                    const float* __restrict__ lse, const float* __restrict__ delta,
-                    float* __restrict__ dq_accum, int S, int BH, int n_tiles, int causal, float scale,
+                    const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ lse,
+                    const float* __restrict__ delta, int S, int BH, int n_tiles, int causal, float scale,
                     float scale_log2, unsigned long long timeout_ns, int* status) {
   using C = BwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -126,14 +131,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sQ = smem + C::kQOff;
   uint8_t* sDO = smem + C::kDOOff;
   uint8_t* sDS = smem + C::kDSOff;
+  uint8_t* sDQ = smem + C::kDQOff;
   float* sLse = reinterpret_cast<float*>(smem + C::kLseOff);
   float* sDelta = reinterpret_cast<float*>(smem + C::kDeltaOff);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
-  uint64_t* do_full = q_full + C::kQStages;
-  uint64_t* qdo_empty = do_full + C::kQStages;
-  uint64_t* ld_full = qdo_empty + C::kQStages;
+  uint64_t* q_empty = q_full + 2;
+  uint64_t* do_full = q_empty + 2;
+  uint64_t* do_empty = do_full + 1;
+  uint64_t* ld_full = do_empty + 1;
   uint64_t* ld_empty = ld_full + 2;
   uint64_t* s_full = ld_empty + 2;
   uint64_t* dp_full = s_full + 1;
@@ -142,20 +149,21 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* ds_empty = ds_ready + 1;
   uint64_t* dq_full = ds_empty + 1;
   uint64_t* dq_empty = dq_full + 1;
-  uint64_t* dkdv_done = dq_empty + 1;
+  uint64_t* stage_full = dq_empty + 1;
+  uint64_t* stage_free = stage_full + 1;
+  uint64_t* dkdv_done = stage_free + 1;
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int i = 0; i < C::kQStages; ++i) {
-      mbar_init(&q_full[i], 1);
-      mbar_init(&do_full[i], 1);
-      mbar_init(&qdo_empty[i], 1);
-    }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&ld_full[i], 32);
       mbar_init(&ld_empty[i], 4);
     }
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
     mbar_init(p_ready, 4);
@@ -163,6 +171,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
+    mbar_init(stage_full, 4);
+    mbar_init(stage_free, 1);
     mbar_init(dkdv_done, 1);
     ctl->abort = 0;
     fence_mbarrier_init();
@@ -174,6 +184,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_map(&tm_do);
     tma_prefetch_map(&tm_dk);
     tma_prefetch_map(&tm_dv);
+    tma_prefetch_map(&tm_dq);
   }
   if (warp == 1) tmem_alloc(&ctl->tmem_base, C::kTmemCols);
   tc_fence_before();
@@ -194,23 +205,24 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     for (int it = 0; it < n_steps; ++it) {
       const int m0 = (i_start + it) * kTileRows;
-      const int st = it % C::kQStages;
-      const uint32_t ph = (it / C::kQStages) & 1;
-      if (!warp_wait(&qdo_empty[st], ph ^ 1, ctl, timeout_ns, status, 1)) break;
+      const int st = it & 1;
+      if (!warp_wait(&q_empty[st], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 1)) break;
       if (lane == 0) {
         mbar_arrive_expect_tx(&q_full[st], C::kTileBytes);
 #pragma unroll
         for (int b = 0; b < D / 64; ++b)
           tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, m0, bh);
-        mbar_arrive_expect_tx(&do_full[st], C::kTileBytes);
+      }
+      if (!warp_wait(do_empty, (it & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(do_full, C::kTileBytes);
 #pragma unroll
-        for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sDO + st * C::kTileBytes + b * kBlockBytes, &tm_do, &do_full[st], b * 64, m0, bh);
+        for (int b = 0; b < D / 64; ++b) tma_load_3d(sDO + b * kBlockBytes, &tm_do, do_full, b * 64, m0, bh);
       }
       // LSE / delta for this query step.  Padded queries get LSE = +inf so
       // their probabilities are exactly zero.
       const int lb = it & 1;
-      if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
+      if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 3)) break;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int q = e * 32 + lane;
@@ -223,19 +235,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    // Order per step i:  dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}.  S_{i+1} goes
-    // out as soon as dV_i has consumed P_i from the S columns, so the dS
-    // warps compute P_{i+1} (the exp2-heavy half of their work) while the
-    // tensor core runs dK_i and dQ_i.
     if (lane == 0) {
       const uint32_t fmt = kBf16 ? 1u : 0u;
       const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
       const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
-      const uint32_t idesc_dq = C::kDqTransposed ? idesc_f16(fmt, D, 128, 1, 1) : idesc_f16(fmt, 128, D, 1, 1);
+      const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
       const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sDSa = smem_u32(sDS);
+      const uint32_t sDOa = smem_u32(sDO);
       auto issue_s = [&](int it) -> bool {
-        const int st = it % C::kQStages;
-        if (!mbar_wait(&q_full[st], (it / C::kQStages) & 1, ctl, timeout_ns, status, 4)) return false;
+        const int st = it & 1;
+        if (!mbar_wait(&q_full[st], (it >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
         tc_fence_after();
         const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
 #pragma unroll
@@ -246,13 +255,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         return true;
       };
       auto issue_dp = [&](int it) -> bool {
-        const int st = it % C::kQStages;
-        if (!mbar_wait(&do_full[st], (it / C::kQStages) & 1, ctl, timeout_ns, status, 5)) return false;
+        if (!mbar_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
         if (C::kDqAliased && it > 0) {
           if (!mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
         }
         tc_fence_after();
-        const uint32_t sDOa = smem_u32(sDO + st * C::kTileBytes);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
           umma_ss(tmem + C::kColDP, sdesc_kmajor(sVa, kTileRows, kk * 16),
@@ -260,41 +267,36 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         umma_commit(dp_full);
         return true;
       };
-      bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 3);
+      bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 7);
       if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
       for (int it = 0; ok && it < n_steps; ++it) {
-        const int st = it % C::kQStages;
+        const int st = it & 1;
         const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
-        const uint32_t sDOa = smem_u32(sDO + st * C::kTileBytes);
         // dV += P^T dO  (P^T packed in the S columns by the dS warps)
-        if (!(ok = mbar_wait(p_ready, it & 1, ctl, timeout_ns, status, 7))) break;
+        if (!(ok = mbar_wait(p_ready, it & 1, ctl, timeout_ns, status, 8))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTileRows / 16; ++kk)
           umma_ts(tmem + C::kColDV, tmem + C::kColS + kk * 8, sdesc_mnmajor(sDOa, kTileRows, kk * 16),
                   idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(do_empty);
         if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
         // dK += dS^T Q  (dS^T in smem from the dS warps)
-        if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 8))) break;
+        if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < kTileRows / 16; ++kk)
           umma_ss(tmem + C::kColDK, sdesc_kmajor(sDSa, kTileRows, kk * 16),
                   sdesc_mnmajor(sQa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&qdo_empty[st]);
-        // dQ = dS K, or dQ^T = K^T dS^T (head_dim 128)
+        umma_commit(&q_empty[st]);
+        // dQ = dS K
         if (!C::kDqAliased && it > 0) {
-          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 9))) break;
+          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
         }
 #pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk) {
-          if constexpr (C::kDqTransposed)
-            umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sKa, kTileRows, kk * 16),
-                    sdesc_mnmajor(sDSa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
-          else
-            umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
-                    sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kTileRows / 16; ++kk)
+          umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
+                  sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
         umma_commit(dq_full);
         umma_commit(ds_empty);
         if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
@@ -311,8 +313,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int it = 0; it < n_steps; ++it) {
       const int i = i_start + it;
       const int lb = it & 1;
-      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 10))) break;
-      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 11))) break;
+      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 11))) break;
+      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 12))) break;
       tc_fence_after();
       const bool diag = causal && (i == jn);
       const float* lse_s = sLse + lb * 128;
@@ -326,7 +328,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tmem_ld32(t_lane + C::kColS + c * 32, sv);
         tmem_wait_ld();
         reg_fence(sv);
-        uint32_t pp[16];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int q = c * 32 + e;
@@ -335,6 +336,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!key_ok) pv = 0.0f;
           p[c][e] = pv;
         }
+        uint32_t pp[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
         tmem_st16(t_lane + C::kColS + c * 16, pp);
@@ -344,9 +346,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(p_ready);
       // Phase 2: dS^T = P^T (dP^T - delta) -> smem for the dK and dQ MMAs.
-      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 12))) break;
+      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 13))) break;
       if (it > 0) {
-        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 13))) break;
+        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 14))) break;
       }
       tc_fence_after();
 #pragma unroll
@@ -379,7 +381,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     // dV epilogue (staged through Q stage 0, stored by TMA; rows >= S are
     // clipped by the tensor map bounds).
-    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 13);
+    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 15);
     if (ok) {
       tc_fence_after();
       stage_row<D, kBf16>(t_lane + C::kColDV, sQ, t, 1.0f);
@@ -393,68 +395,62 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       tma_store_wait_read_all();
     }
   } else {
-    // ---------------- dQ warps ----------------
-    // head_dim 128: thread r owns head-dim column r of dQ^T and, for every
-    // query m of the step, the 32 lanes of a warp add 32 consecutive floats
-    // (one 128-byte segment of row m).  head_dim 64: thread r owns query
-    // m0 + r and adds its row with 16-byte vector atomics.
+    // ---------------- dQ warps: thread r owns query m0 + r ----------------
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const bool issuer = (warp == 6 && lane == 0);
     bool ok = true;
-    for (int it = 0; it < n_steps; ++it) {
+    for (int it = 0; ok && it < n_steps; ++it) {
       const int m0 = (i_start + it) * kTileRows;
-      if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 14))) break;
+      if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 16))) break;
       tc_fence_after();
-      if constexpr (C::kDqTransposed) {
-        uint32_t v[4][32];
+      uint32_t v[D / 32][32];
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
-        tmem_wait_ld();
+      for (int cb = 0; cb < D / 32; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
+      tmem_wait_ld();
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) reg_fence(v[cb]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dq_empty);
-        float* col = dq_accum + (row_base + m0) * D + r;
-        const int rows = min(kTileRows, S - m0);
+      for (int cb = 0; cb < D / 32; ++cb) reg_fence(v[cb]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
+      for (int pass = 0; pass < C::kDqPasses; ++pass) {
+        const uint32_t cnt = static_cast<uint32_t>(it * C::kDqPasses + pass);
+        if (!(ok = warp_wait(stage_free, (cnt & 1) ^ 1, ctl, timeout_ns, status, 17))) break;
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int m = cb * 32 + e;
-            if (m < rows) atomicAdd(col + static_cast<size_t>(m) * D, __uint_as_float(v[cb][e]) * scale);
+        for (int bx = 0; bx < 2; ++bx) {
+          uint8_t* box = sDQ + bx * kTileRows * kSwizzleBytes;
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) {
+            const float4 w = make_float4(__uint_as_float(v[pass * 2 + bx][ch * 4 + 0]) * scale,
+                                         __uint_as_float(v[pass * 2 + bx][ch * 4 + 1]) * scale,
+                                         __uint_as_float(v[pass * 2 + bx][ch * 4 + 2]) * scale,
+                                         __uint_as_float(v[pass * 2 + bx][ch * 4 + 3]) * scale);
+            *reinterpret_cast<float4*>(box + swz_offset_f32(r, ch * 4)) = w;
           }
         }
-      } else {
-        const int mg = m0 + r;
-        uint32_t v[D / 32][32];
-#pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) tmem_ld32(t_lane + C::kColDQ + cb * 32, v[cb]);
-        tmem_wait_ld();
-#pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) reg_fence(v[cb]);
-        tc_fence_before();
+        fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(dq_empty);
-        if (mg < S) {
-          float4* dst = reinterpret_cast<float4*>(dq_accum + (row_base + mg) * D);
+        if (lane == 0) mbar_arrive(stage_full);
+        bool issued = true;
+        if (issuer) {
+          issued = mbar_wait(stage_full, cnt & 1, ctl, timeout_ns, status, 18);
+          if (issued) {
 #pragma unroll
-          for (int cb = 0; cb < D / 32; ++cb) {
-#pragma unroll
-            for (int f = 0; f < 8; ++f) {
-              const float4 add = make_float4(__uint_as_float(v[cb][4 * f + 0]) * scale,
-                                             __uint_as_float(v[cb][4 * f + 1]) * scale,
-                                             __uint_as_float(v[cb][4 * f + 2]) * scale,
-                                             __uint_as_float(v[cb][4 * f + 3]) * scale);
-              atomicAdd(dst + cb * 8 + f, add);
-            }
+            for (int bx = 0; bx < 2; ++bx)
+              tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
+            tma_store_commit();
+            tma_store_wait_read_all();
+            mbar_arrive(stage_free);
           }
         }
+        if (!(ok = __all_sync(0xffffffffu, issued))) break;
       }
     }
-    // dK epilogue (staged through dO stage 0).
-    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 13);
+    if (issuer) tma_store_wait_all();
+    // dK epilogue (staged through the dO buffer).
+    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 19);
     if (ok) {
       tc_fence_after();
       stage_row<D, kBf16>(t_lane + C::kColDK, sDO, r, scale);
@@ -495,7 +491,7 @@ int launch_bwd_t(const BwdArgs& a) {
   const int n_tiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
   const long long grid = static_cast<long long>(n_tiles) * a.BH;
   kern<<<static_cast<unsigned>(grid), kBwdThreads, C::kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, *a.tm_dk, *a.tm_dv, a.lse, a.delta, a.dq_accum,
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, *a.tm_dk, *a.tm_dv, *a.tm_dq, a.lse, a.delta,
       static_cast<int>(a.S), static_cast<int>(a.BH), n_tiles, a.causal, a.scale, a.scale_log2,
       a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;

@@ -85,6 +85,24 @@ int make_map(CUtensorMap* map, const void* base, int64_t bh, int64_t seq, int64_
   return r == CUDA_SUCCESS ? tk::kOk : tk::kErrTensorMap;
 }
 
+// 3-D map over the contiguous fp32 (B*H, S, D) dQ accumulator: box
+// {32, 128, 1} (128-byte rows) with the 128-byte swizzle; used as the target
+// of TMA bulk reduce-add.
+int make_map_f32(CUtensorMap* map, const float* base, int64_t bh, int64_t seq, int64_t head_dim) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return tk::kErrNoDriver;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq),
+                        static_cast<cuuint64_t>(bh)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * 4),
+                           static_cast<cuuint64_t>(seq * head_dim * 4)};
+  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? tk::kOk : tk::kErrTensorMap;
+}
+
 constexpr float kLog2e = 1.4426950408889634f;
 
 }  // namespace
@@ -142,14 +160,15 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   int* status = nullptr;
   if (int rc = status_ptr(&status)) return rc;
   const int64_t bh = batch * heads;
-  CUtensorMap mq, mk, mv, mdo, mdk, mdv;
+  CUtensorMap mq, mk, mv, mdo, mdk, mdv, mdq;
   if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mdo, d_o, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mdk, dk, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mdv, dv, bh, seq, head_dim, dtype)) return rc;
-  tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, lse, delta, dq_accum,
+  if (int rc = make_map_f32(&mdq, dq_accum, bh, seq, head_dim)) return rc;
+  tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, &mdq, lse, delta,
                 bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
                 scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
   return tk::launch_attn_bwd(a);

@@ -40,9 +40,9 @@ struct BwdArgs {
   const CUtensorMap* tm_do;
   const CUtensorMap* tm_dk;
   const CUtensorMap* tm_dv;
+  const CUtensorMap* tm_dq;  // fp32 dQ accumulator, reduced into by TMA
   const float* lse;
   const float* delta;
-  float* dq_accum;
   int64_t BH, S, D;
   bool bf16;
   int causal;

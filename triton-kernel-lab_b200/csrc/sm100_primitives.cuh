@@ -156,6 +156,28 @@ __device__ __forceinline__ void tma_store_wait_read_all() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
+// Wait until every committed bulk group has fully completed (writes done).
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Element-wise add of a shared-memory box into global memory (fp32 map),
+// performed by the TMA unit; elements outside the tensor are skipped.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1, int c2) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], "
+      "[%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Byte offset of fp32 element (row, col) inside one 128-byte-wide box
+// (32 floats per row) stored with the 128-byte swizzle.
+__device__ __forceinline__ uint32_t swz_offset_f32(uint32_t row, uint32_t col) {
+  return row * kSwizzleBytes + ((((col >> 2) & 7u) ^ (row & 7u)) << 4) + ((col & 3u) << 2);
+}
+
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (TMA store, tcgen05.mma operand reads).
 __device__ __forceinline__ void fence_proxy_async_smem() {
