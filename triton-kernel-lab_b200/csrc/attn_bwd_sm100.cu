@@ -17,17 +17,20 @@
 //
 // One CTA owns a 128-key tile (K, V resident in smem) of one (batch, head)
 // and walks 128-query steps.  The transposed products are computed directly
-// (S^T = K Q^T, dP^T = V dO^T) so TMEM lane n holds key n:
-//   warp 0      producer: TMA for K, V, Q_i (2 stages), dO_i (1 stage);
-//               plain loads of LSE/delta
-//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 2..5  "dS warps": thread n owns key n.  Phase 1: P^T for the 128
-//               queries of a step, written back as 16-bit over the S^T
-//               columns for the dV MMA.  Phase 2: dS^T = P^T (dP^T - delta)
-//               to smem for the dK and dQ MMAs.  dV epilogue.
-//   warps 6..9  "dQ warps": thread m owns query m of the step; copy dQ from
-//               TMEM into an fp32 staging tile (32 KB, 128-byte swizzle);
-//               warp 6 lane 0 issues the TMA reduce-add.  dK epilogue.
+// (S^T = K Q^T, dP^T = V dO^T) so TMEM lane n holds key n.  16 warps in four
+// warpgroups, registers rebalanced with setmaxnreg:
+//   WG0  warp 0   producer: TMA for K, V, Q_i (2 stages), dO_i (1 stage);
+//                 plain loads of LSE/delta
+//        warp 1   TMEM allocator and single-thread tcgen05.mma issuer
+//        warp 2   issues the TMA reduce-add of each staged dQ tile
+//   WG1  warps 4..7   "dQ warps": thread m owns query m of the step; copy dQ
+//                     from TMEM into an fp32 staging tile (128-byte swizzle)
+//   WG2, WG3  warps 8..15  "dS warps": WG2 owns queries 0..63 of a step,
+//                     WG3 queries 64..127; thread t owns key t.  Phase 1:
+//                     P^T, packed to 16 bits over the first half of the
+//                     warpgroup's own S^T columns for the dV MMA.  Phase 2:
+//                     dS^T = P^T (dP^T - delta) to smem for the dK and dQ
+//                     MMAs.  Epilogue: WG2 stores dV, WG3 stores dK.
 // MMA issue order per step i: dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}, so the dS
 // warps compute P_{i+1} (the exp2-heavy phase) while dK_i and dQ_i run.
 // TMEM columns: dV [0,D) dK [D,2D) S^T/P^T [2D,2D+128) dP^T [2D+128,2D+256);
@@ -70,7 +73,15 @@ struct BwdCfg {
   static constexpr int kDqPasses = D / 64;
 };
 
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 512;
+// Launch allocation 128 registers x 512 threads = 65536; per warpgroup after
+// setmaxnreg: WG0 56 + WG1 152 + WG2 152 + WG3 152 = 512 x 128 threads, which
+// never exceeds the launch allocation (an inc beyond it would never return).
+constexpr int kBwdLaunchRegs = 128;
+constexpr int kRegsCtrl = 56;
+constexpr int kRegsDq = 152;
+constexpr int kRegsDs = 152;
+static_assert(kRegsCtrl + kRegsDq + 2 * kRegsDs <= 4 * kBwdLaunchRegs, "register split exceeds the launch");
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaControl* ctl,
                                           uint64_t timeout_ns, int* status, int site) {
@@ -100,6 +111,31 @@ __device__ __forceinline__ void stage_row(uint32_t t_row, uint8_t* tile, int r, 
   }
 }
 
+// P^T for 32 queries of one key row: p = exp2(s * scale*log2(e) - LSE2[q]).
+// The 32 LSE values are read with 128-bit broadcast loads (every lane of the
+// warp reads the same address).  kMasked adds the causal diagonal (query q0+e
+// is dropped when it precedes this thread's key, diag_key) and the ragged key
+// tail (key_ok false: the whole row is zero).
+template <bool kMasked>
+__device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const float* lse_s, float scale_log2,
+                                            int q0, int diag_key, bool key_ok, float (&p)[32]) {
+  const float4* lse4 = reinterpret_cast<const float4*>(lse_s);
+#pragma unroll
+  for (int e4 = 0; e4 < 8; ++e4) {
+    const float4 l = lse4[e4];
+    const float lv[4] = {l.x, l.y, l.z, l.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = e4 * 4 + j;
+      float pv = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lv[j]));
+      if constexpr (kMasked) {
+        if (q0 + e < diag_key || !key_ok) pv = 0.0f;
+      }
+      p[e] = pv;
+    }
+  }
+}
+
 template <int D, bool kBf16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -116,6 +152,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int wg = warp >> 2;
   // Head-major order: the key tiles of one (batch, head) are adjacent in the
   // grid, so resident CTAs share a few heads' Q, dO and dQ-accumulator lines
   // in L2.  Within a head the key tiles with the most query steps (smallest
@@ -160,14 +197,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&ld_full[i], 32);
-      mbar_init(&ld_empty[i], 4);
+      mbar_init(&ld_empty[i], 8);
     }
     mbar_init(do_full, 1);
     mbar_init(do_empty, 1);
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_ready, 4);
-    mbar_init(ds_ready, 4);
+    mbar_init(p_ready, 8);
+    mbar_init(ds_ready, 8);
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
@@ -193,216 +230,149 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tmem = ctl->tmem_base;
   const size_t row_base = static_cast<size_t>(bh) * S;
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
-#pragma unroll
-      for (int b = 0; b < D / 64; ++b) {
-        tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
-        tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
-      }
-    }
-    for (int it = 0; it < n_steps; ++it) {
-      const int m0 = (i_start + it) * kTileRows;
-      const int st = it & 1;
-      if (!warp_wait(&q_empty[st], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 1)) break;
+  if (wg == 0) {
+    warpgroup_reg_dec<kRegsCtrl>();
+    if (warp == 0) {
+      // ---------------- producer ----------------
       if (lane == 0) {
-        mbar_arrive_expect_tx(&q_full[st], C::kTileBytes);
+        mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
 #pragma unroll
-        for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, m0, bh);
-      }
-      if (!warp_wait(do_empty, (it & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(do_full, C::kTileBytes);
-#pragma unroll
-        for (int b = 0; b < D / 64; ++b) tma_load_3d(sDO + b * kBlockBytes, &tm_do, do_full, b * 64, m0, bh);
-      }
-      // LSE / delta for this query step.  Padded queries get LSE = +inf so
-      // their probabilities are exactly zero.
-      const int lb = it & 1;
-      if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 3)) break;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int q = e * 32 + lane;
-        const int mg = m0 + q;
-        const bool valid = mg < S;
-        sLse[lb * 128 + q] = valid ? lse[row_base + mg] : INFINITY;
-        sDelta[lb * 128 + q] = valid ? delta[row_base + mg] : 0.0f;
-      }
-      mbar_arrive(&ld_full[lb]);
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t fmt = kBf16 ? 1u : 0u;
-      const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
-      const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
-      const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
-      const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sDSa = smem_u32(sDS);
-      const uint32_t sDOa = smem_u32(sDO);
-      auto issue_s = [&](int it) -> bool {
-        const int st = it & 1;
-        if (!mbar_wait(&q_full[st], (it >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
-        tc_fence_after();
-        const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + C::kColS, sdesc_kmajor(sKa, kTileRows, kk * 16),
-                  sdesc_kmajor(sQa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit(s_full);
-        return true;
-      };
-      auto issue_dp = [&](int it) -> bool {
-        if (!mbar_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
-        if (C::kDqAliased && it > 0) {
-          if (!mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
+        for (int b = 0; b < D / 64; ++b) {
+          tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
+          tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
         }
-        tc_fence_after();
+      }
+      for (int it = 0; it < n_steps; ++it) {
+        const int m0 = (i_start + it) * kTileRows;
+        const int st = it & 1;
+        if (!warp_wait(&q_empty[st], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 1)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&q_full[st], C::kTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + C::kColDP, sdesc_kmajor(sVa, kTileRows, kk * 16),
-                  sdesc_kmajor(sDOa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit(dp_full);
-        return true;
-      };
-      bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 7);
-      if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
+          for (int b = 0; b < D / 64; ++b)
+            tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, m0, bh);
+        }
+        if (!warp_wait(do_empty, (it & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(do_full, C::kTileBytes);
+#pragma unroll
+          for (int b = 0; b < D / 64; ++b) tma_load_3d(sDO + b * kBlockBytes, &tm_do, do_full, b * 64, m0, bh);
+        }
+        // LSE / delta for this query step.  Padded queries get LSE = +inf so
+        // their probabilities are exactly zero.
+        const int lb = it & 1;
+        if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 3)) break;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int q = e * 32 + lane;
+          const int mg = m0 + q;
+          const bool valid = mg < S;
+          sLse[lb * 128 + q] = valid ? lse[row_base + mg] : INFINITY;
+          sDelta[lb * 128 + q] = valid ? delta[row_base + mg] : 0.0f;
+        }
+        mbar_arrive(&ld_full[lb]);
+      }
+    } else if (warp == 1) {
+      // ---------------- MMA issuer ----------------
+      if (lane == 0) {
+        const uint32_t fmt = kBf16 ? 1u : 0u;
+        const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
+        const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
+        const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
+        const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sDSa = smem_u32(sDS);
+        const uint32_t sDOa = smem_u32(sDO);
+        auto issue_s = [&](int it) -> bool {
+          const int st = it & 1;
+          if (!mbar_wait(&q_full[st], (it >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
+          tc_fence_after();
+          const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ss(tmem + C::kColS, sdesc_kmajor(sKa, kTileRows, kk * 16),
+                    sdesc_kmajor(sQa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
+          umma_commit(s_full);
+          return true;
+        };
+        auto issue_dp = [&](int it) -> bool {
+          if (!mbar_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
+          if (C::kDqAliased && it > 0) {
+            if (!mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ss(tmem + C::kColDP, sdesc_kmajor(sVa, kTileRows, kk * 16),
+                    sdesc_kmajor(sDOa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
+          umma_commit(dp_full);
+          return true;
+        };
+        bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 7);
+        if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
+        for (int it = 0; ok && it < n_steps; ++it) {
+          const int st = it & 1;
+          const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
+          // dV += P^T dO.  P^T of queries 64h..64h+63 sits packed in the
+          // first 32 columns of warpgroup h's 64 S columns.
+          if (!(ok = mbar_wait(p_ready, it & 1, ctl, timeout_ns, status, 8))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ts(tmem + C::kColDV, tmem + C::kColS + (kk >> 2) * 64 + (kk & 3) * 8,
+                    sdesc_mnmajor(sDOa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(do_empty);
+          if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
+          // dK += dS^T Q  (dS^T in smem from the dS warps)
+          if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ss(tmem + C::kColDK, sdesc_kmajor(sDSa, kTileRows, kk * 16),
+                    sdesc_mnmajor(sQa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&q_empty[st]);
+          // dQ = dS K
+          if (!C::kDqAliased && it > 0) {
+            if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
+          }
+#pragma unroll
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
+                    sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
+          umma_commit(dq_full);
+          umma_commit(ds_empty);
+          if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
+        }
+        if (ok) umma_commit(dkdv_done);
+      }
+    } else if (warp == 2) {
+      // ---------------- dQ reduce issuer ----------------
+      bool ok = true;
       for (int it = 0; ok && it < n_steps; ++it) {
-        const int st = it & 1;
-        const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
-        // dV += P^T dO  (P^T packed in the S columns by the dS warps)
-        if (!(ok = mbar_wait(p_ready, it & 1, ctl, timeout_ns, status, 8))) break;
-        tc_fence_after();
+        const int m0 = (i_start + it) * kTileRows;
 #pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk)
-          umma_ts(tmem + C::kColDV, tmem + C::kColS + kk * 8, sdesc_mnmajor(sDOa, kTileRows, kk * 16),
-                  idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(do_empty);
-        if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
-        // dK += dS^T Q  (dS^T in smem from the dS warps)
-        if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
-        tc_fence_after();
+        for (int pass = 0; pass < C::kDqPasses; ++pass) {
+          const uint32_t cnt = static_cast<uint32_t>(it * C::kDqPasses + pass);
+          if (!(ok = warp_wait(stage_full, cnt & 1, ctl, timeout_ns, status, 18))) break;
+          if (lane == 0) {
 #pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk)
-          umma_ss(tmem + C::kColDK, sdesc_kmajor(sDSa, kTileRows, kk * 16),
-                  sdesc_mnmajor(sQa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&q_empty[st]);
-        // dQ = dS K
-        if (!C::kDqAliased && it > 0) {
-          if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
-        }
-#pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk)
-          umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
-                  sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
-        umma_commit(dq_full);
-        umma_commit(ds_empty);
-        if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
-      }
-      if (ok) umma_commit(dkdv_done);
-    }
-  } else if (warp < 6) {
-    // ---------------- dS warps: thread t owns key n0 + t ----------------
-    const int q4 = warp & 3;
-    const int t = q4 * 32 + lane;
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    const bool key_ok = (n0 + t) < S;
-    bool ok = true;
-    for (int it = 0; it < n_steps; ++it) {
-      const int i = i_start + it;
-      const int lb = it & 1;
-      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 11))) break;
-      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 12))) break;
-      tc_fence_after();
-      const bool diag = causal && (i == jn);
-      const float* lse_s = sLse + lb * 128;
-      const float* del_s = sDelta + lb * 128;
-      // Phase 1: P^T row (all 128 queries of the step) -> registers and,
-      // packed to 16 bits, back over the S columns for the dV MMA.
-      float p[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tmem_ld32(t_lane + C::kColS + c * 32, sv);
-        tmem_wait_ld();
-        reg_fence(sv);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int q = c * 32 + e;
-          float pv = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lse_s[q]));
-          if (diag && q < t) pv = 0.0f;
-          if (!key_ok) pv = 0.0f;
-          p[c][e] = pv;
-        }
-        uint32_t pp[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
-        tmem_st16(t_lane + C::kColS + c * 16, pp);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_ready);
-      // Phase 2: dS^T = P^T (dP^T - delta) -> smem for the dK and dQ MMAs.
-      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 13))) break;
-      if (it > 0) {
-        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 14))) break;
-      }
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t dpv[32];
-        tmem_ld32(t_lane + C::kColDP + c * 32, dpv);
-        tmem_wait_ld();
-        reg_fence(dpv);
-        uint32_t dd[16];
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int q = c * 32 + e;
-          const float d0 = p[c][e] * (__uint_as_float(dpv[e]) - del_s[q]);
-          const float d1 = p[c][e + 1] * (__uint_as_float(dpv[e + 1]) - del_s[q + 1]);
-          dd[e >> 1] = pack2<kBf16>(d0, d1);
-        }
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          uint4 v = make_uint4(dd[w * 4 + 0], dd[w * 4 + 1], dd[w * 4 + 2], dd[w * 4 + 3]);
-          *reinterpret_cast<uint4*>(sDS + swz_offset(t, c * 32 + w * 8, kTileRows)) = v;
+            for (int bx = 0; bx < 2; ++bx)
+              tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
+            tma_store_commit();
+            tma_store_wait_read_all();
+            mbar_arrive(stage_free);
+          }
+          __syncwarp();
         }
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&ld_empty[lb]);
-        mbar_arrive(ds_ready);
-      }
+      if (lane == 0) tma_store_wait_all();
     }
-    // dV epilogue (staged through Q stage 0, stored by TMA; rows >= S are
-    // clipped by the tensor map bounds).
-    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 15);
-    if (ok) {
-      tc_fence_after();
-      stage_row<D, kBf16>(t_lane + C::kColDV, sQ, t, 1.0f);
-      fence_proxy_async_smem();
-    }
-    named_barrier_sync(1, 128);
-    if (warp == 2 && lane == 0 && !ctl->abort) {
-#pragma unroll
-      for (int b = 0; b < D / 64; ++b) tma_store_3d(&tm_dv, sQ + b * kBlockBytes, b * 64, n0, bh);
-      tma_store_commit();
-      tma_store_wait_read_all();
-    }
-  } else {
+  } else if (wg == 1) {
+    warpgroup_reg_inc<kRegsDq>();
     // ---------------- dQ warps: thread r owns query m0 + r ----------------
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    const bool issuer = (warp == 6 && lane == 0);
     bool ok = true;
     for (int it = 0; ok && it < n_steps; ++it) {
-      const int m0 = (i_start + it) * kTileRows;
       if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 16))) break;
       tc_fence_after();
       uint32_t v[D / 32][32];
@@ -433,33 +403,107 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(stage_full);
-        bool issued = true;
-        if (issuer) {
-          issued = mbar_wait(stage_full, cnt & 1, ctl, timeout_ns, status, 18);
-          if (issued) {
-#pragma unroll
-            for (int bx = 0; bx < 2; ++bx)
-              tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
-            tma_store_commit();
-            tma_store_wait_read_all();
-            mbar_arrive(stage_free);
-          }
-        }
-        if (!(ok = __all_sync(0xffffffffu, issued))) break;
       }
     }
-    if (issuer) tma_store_wait_all();
-    // dK epilogue (staged through the dO buffer).
-    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 19);
+  } else {
+    warpgroup_reg_inc<kRegsDs>();
+    // ---------------- dS warps: thread t owns key n0 + t ----------------
+    const int h = wg - 2;  // query half of the step owned by this warpgroup
+    const int q4 = warp & 3;
+    const int t = q4 * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const uint32_t s_cols = t_lane + C::kColS + h * 64;
+    const uint32_t dp_cols = t_lane + C::kColDP + h * 64;
+    const bool key_ok = (n0 + t) < S;
+    bool ok = true;
+    for (int it = 0; it < n_steps; ++it) {
+      const int i = i_start + it;
+      const int lb = it & 1;
+      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 11))) break;
+      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 12))) break;
+      tc_fence_after();
+      const bool diag = causal && (i == jn);
+      const float* lse_s = sLse + lb * 128 + h * 64;
+      const float* del_s = sDelta + lb * 128 + h * 64;
+      // Phase 1: P^T for this warpgroup's 64 queries -> registers and,
+      // packed to 16 bits, back over the first 32 of its S columns (each
+      // 32-column chunk is read before its packed half is written).
+      float p[2][32];
+      const bool masked = __any_sync(0xffffffffu, diag || !key_ok);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32];
+        tmem_ld32(s_cols + c * 32, sv);
+        tmem_wait_ld();
+        reg_fence(sv);
+        if (masked)
+          probs_chunk<true>(sv, lse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
+        else
+          probs_chunk<false>(sv, lse_s + c * 32, scale_log2, 0, 0, true, p[c]);
+        uint32_t pp[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
+        tmem_st16(s_cols + c * 16, pp);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // Phase 2: dS^T = P^T (dP^T - delta) -> smem for the dK and dQ MMAs.
+      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 13))) break;
+      if (it > 0) {
+        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 14))) break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t dpv[32];
+        tmem_ld32(dp_cols + c * 32, dpv);
+        tmem_wait_ld();
+        reg_fence(dpv);
+        uint32_t dd[16];
+        const float4* del4 = reinterpret_cast<const float4*>(del_s + c * 32);
+#pragma unroll
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 dl = del4[e4];  // one broadcast 128-bit load for 4 queries
+          const int e = e4 * 4;
+          dd[e4 * 2] = pack2<kBf16>(p[c][e] * (__uint_as_float(dpv[e]) - dl.x),
+                                    p[c][e + 1] * (__uint_as_float(dpv[e + 1]) - dl.y));
+          dd[e4 * 2 + 1] = pack2<kBf16>(p[c][e + 2] * (__uint_as_float(dpv[e + 2]) - dl.z),
+                                        p[c][e + 3] * (__uint_as_float(dpv[e + 3]) - dl.w));
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint4 v = make_uint4(dd[w * 4 + 0], dd[w * 4 + 1], dd[w * 4 + 2], dd[w * 4 + 3]);
+          *reinterpret_cast<uint4*>(sDS + swz_offset(t, h * 64 + c * 32 + w * 8, kTileRows)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&ld_empty[lb]);
+        mbar_arrive(ds_ready);
+      }
+    }
+    // Epilogue: WG2 stores dV (staged through Q stage 0), WG3 stores dK
+    // (scaled, staged through the dO buffer).  Rows >= S are clipped by the
+    // tensor map bounds.
+    uint8_t* stage = (h == 0) ? sQ : sDO;
+    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 15);
     if (ok) {
       tc_fence_after();
-      stage_row<D, kBf16>(t_lane + C::kColDK, sDO, r, scale);
+      if (h == 0)
+        stage_row<D, kBf16>(t_lane + C::kColDV, stage, t, 1.0f);
+      else
+        stage_row<D, kBf16>(t_lane + C::kColDK, stage, t, scale);
       fence_proxy_async_smem();
     }
-    named_barrier_sync(2, 128);
-    if (warp == 6 && lane == 0 && !ctl->abort) {
+    named_barrier_sync(1 + h, 128);
+    if ((warp & 3) == 0 && lane == 0 && !ctl->abort) {
+      const CUtensorMap* map = (h == 0) ? &tm_dv : &tm_dk;
 #pragma unroll
-      for (int b = 0; b < D / 64; ++b) tma_store_3d(&tm_dk, sDO + b * kBlockBytes, b * 64, n0, bh);
+      for (int b = 0; b < D / 64; ++b) tma_store_3d(map, stage + b * kBlockBytes, b * 64, n0, bh);
       tma_store_commit();
       tma_store_wait_read_all();
     }
@@ -483,6 +527,11 @@ int launch_bwd_t(const BwdArgs& a) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
+    // The setmaxnreg split inside the kernel assumes exactly kBwdLaunchRegs
+    // registers per thread at launch; refuse to run a build that differs.
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, kern) != cudaSuccess || attr.numRegs != kBwdLaunchRegs)
+      return kErrLaunch;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
         cudaSuccess)
       return kErrLaunch;
