@@ -23,6 +23,7 @@
 //                 plain loads of LSE/delta
 //        warp 1   TMEM allocator and single-thread tcgen05.mma issuer
 //        warp 2   issues the TMA reduce-add of each staged dQ tile
+//        warp 3   producer of the Q tiles
 //   WG1  warps 4..7   "dQ warps": thread m owns query m of the step; copy dQ
 //                     from TMEM into an fp32 staging tile (128-byte swizzle)
 //   WG2, WG3  warps 8..15  "dS warps": WG2 owns queries 0..63 of a step,
@@ -232,16 +233,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (wg == 0) {
     warpgroup_reg_dec<kRegsCtrl>();
-    if (warp == 0) {
-      // ---------------- producer ----------------
-      if (lane == 0) {
-        mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
-#pragma unroll
-        for (int b = 0; b < D / 64; ++b) {
-          tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
-          tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
-        }
-      }
+    if (warp == 3) {
+      // ---------------- Q producer (its own warp so a Q load never waits
+      // behind the dO or LSE waits) ----------------
       for (int it = 0; it < n_steps; ++it) {
         const int m0 = (i_start + it) * kTileRows;
         const int st = it & 1;
@@ -252,6 +246,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int b = 0; b < D / 64; ++b)
             tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, m0, bh);
         }
+      }
+    } else if (warp == 0) {
+      // ---------------- K/V, dO and LSE/delta producer ----------------
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b) {
+          tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
+          tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
+        }
+      }
+      for (int it = 0; it < n_steps; ++it) {
+        const int m0 = (i_start + it) * kTileRows;
         if (!warp_wait(do_empty, (it & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
         if (lane == 0) {
           mbar_arrive_expect_tx(do_full, C::kTileBytes);
