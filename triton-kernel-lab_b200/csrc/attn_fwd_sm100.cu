@@ -1,7 +1,7 @@
 // Flash-attention forward for sm_100a (B200): TMA-fed Q/K/V tiles, tcgen05
 // MMAs accumulating S = Q.K^T and O += P.V in tensor memory, online softmax
 // in base 2 with the scale folded in, causal tile skipping and a separate
-// masked path for the diagonal / ragged-tail key tile.
+// masked path for the diagonal / ragged-tail key tiles.
 //
 // Semantics follow the reference Triton kernel
 // (src/tklab/kernels/flash_attention.py:54-117 `_attention_inner` and
@@ -11,16 +11,23 @@
 // for the P.V product, O = acc / row_sum, and the optional statistic is the
 // base-2 log-sum-exp `row_max + log2(row_sum)` (:254-264).
 //
-// One CTA owns one 128-row query tile of one (batch, head).  Warp roles:
-//   warp 0      TMA producer (Q once, then K and V tiles through a ring)
-//   warp 1      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 2..5  softmax: thread t owns query row t (= TMEM lane t), also
-//               rescales O when the running maximum moves, and runs the
-//               epilogue (normalise, stage in smem, TMA store, LSE store).
-// Tensor memory (512 columns): O at [0, D), two S buffers of 128 columns at
-// 128 and 256 so the MMA warp computes S(j+1) while softmax works on S(j).
-// P(j) is written back as packed 16-bit pairs over the first 64 columns of
-// its own S buffer and consumed from TMEM by the P.V MMA.
+// One CTA owns two consecutive 128-row query tiles (A and B) of one
+// (batch, head) and streams the key/value tiles once for both.  12 warps in
+// three warpgroups, registers rebalanced with setmaxnreg:
+//   WG0  warp 0   TMA producer (Q_A and Q_B once, then K and V tiles
+//                 through two rings)
+//        warp 1   TMEM allocator and single-thread tcgen05.mma issuer
+//   WG1  warps 4..7   softmax of tile A: thread t owns query row t (TMEM
+//                     lane t); also rescales O_A when its running maximum
+//                     moves, and runs tile A's epilogue
+//   WG2  warps 8..11  the same for tile B
+// Tensor memory (512 columns): O_A, O_B (D columns each), then S_A and S_B
+// (128 columns each).  P is written back as packed 16-bit pairs over the
+// first 64 columns of its tile's S and consumed from TMEM by the P.V MMA.
+// MMA issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so
+// while the softmax of one tile runs the tensor core works on the other
+// tile.  S_X(j+1) is issued after PV_X(j), so once a softmax warpgroup sees
+// S_X(j+1) complete it may rescale O_X without a separate barrier.
 #include "attn_launch.h"
 #include "sm100_primitives.cuh"
 
@@ -31,22 +38,29 @@ template <int D>
 struct FwdCfg {
   static constexpr int kStages = (D == 64) ? 4 : 2;
   static constexpr int kTileBytes = kTileRows * D * 2;
-  static constexpr int kQOff = 0;
-  static constexpr int kKOff = kQOff + kTileBytes;
+  static constexpr int kQOff = 0;  // Q_A, Q_B
+  static constexpr int kKOff = kQOff + 2 * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2],
-  // p_ready[2], o_done, o_final
-  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 2;
+  // p_ready[2], o_final[2]
+  static constexpr int kNumBars = 1 + 4 * kStages + 6;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kColO = 0;
-  // S buffer b (0 or 1) starts at column kColS0 + 128 * b.
-  static constexpr uint32_t kColS0 = 128;
+  // O of tile x at column x * D, S of tile x at 2D + 128 x.
+  static constexpr uint32_t kColO0 = 0;
+  static constexpr uint32_t kColS0 = 2 * D;
 };
 
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 384;
+// Launch allocation 168 registers x 384 threads; after setmaxnreg the control
+// warpgroup keeps 56 and each softmax warpgroup gets 224 (56 + 2 x 224 =
+// 3 x 168), so the increases are always satisfiable.
+constexpr int kFwdLaunchRegs = 168;
+constexpr int kFwdRegsCtrl = 56;
+constexpr int kFwdRegsSoftmax = 224;
+static_assert(kFwdRegsCtrl + 2 * kFwdRegsSoftmax <= 3 * kFwdLaunchRegs, "register split exceeds the launch");
 // The running maximum used for P is only moved when the true maximum exceeds
 // it by more than this (base-2 units), so P <= 2^8 and O is rescaled rarely.
 // The result is unchanged mathematically because O and row_sum always share
@@ -59,10 +73,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaCon
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int D, bool kBf16, bool kMasked>
+// Online-softmax step for one row and one 128-key tile held in s[4][32]:
+// updates the running maximum / sum, returns the rescale factor of the
+// previous accumulator (alpha) and whether the maximum moved (need), and
+// writes P (16-bit pairs) over the first 64 TMEM columns at s_addr.
+template <bool kBf16, bool kMasked>
 __device__ __forceinline__ void softmax_tile(uint32_t (&s)[4][32], int lim, float scale_log2,
-                                             float& m_run, float& l_run, float& alpha,
-                                             bool& need, uint32_t (&pk)[2][32]) {
+                                             float& m_run, float& l_run, float& alpha, bool& need,
+                                             uint32_t s_addr) {
   float mx = -INFINITY;
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
@@ -86,14 +104,16 @@ __device__ __forceinline__ void softmax_tile(uint32_t (&s)[4][32], int lim, floa
   float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
+    uint32_t pk[16];
 #pragma unroll
     for (int c = 0; c < 32; c += 2) {
       const float p0 = ex2(fmaf(__uint_as_float(s[b][c]), scale_log2, -ms));
       const float p1 = ex2(fmaf(__uint_as_float(s[b][c + 1]), scale_log2, -ms));
       sum0 += p0;
       sum1 += p1;
-      pk[b >> 1][(b & 1) * 16 + (c >> 1)] = pack2<kBf16>(p0, p1);
+      pk[c >> 1] = pack2<kBf16>(p0, p1);
     }
+    tmem_st16(s_addr + b * 16, pk);
   }
   l_run = l_run * alpha + (sum0 + sum1);
   m_run = m_use;
@@ -103,8 +123,8 @@ template <int D, bool kBf16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    float* __restrict__ lse, int S, int BH, int n_mtiles, int causal,
-                    float scale_log2, unsigned long long timeout_ns, int* status) {
+                    float* __restrict__ lse, int S, int BH, int n_ctiles, int causal, float scale_log2,
+                    unsigned long long timeout_ns, int* status) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -113,15 +133,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  // Head-major order: the query tiles of one (batch, head) are adjacent in
-  // the grid, so the CTAs resident at any time share a few heads' K/V in L2.
-  // Within a head the heaviest tiles (largest index under a causal mask)
-  // launch first.
-  const int bh = static_cast<int>(blockIdx.x) / n_mtiles;
-  const int mt = n_mtiles - 1 - static_cast<int>(blockIdx.x) % n_mtiles;
-  const int m0 = mt * kTileRows;
+  const int wg = warp >> 2;
+  // Head-major order: the query-tile pairs of one (batch, head) are adjacent
+  // in the grid, so the CTAs resident at any time share a few heads' K/V in
+  // L2.  Within a head the heaviest pairs (largest index under a causal
+  // mask) launch first.
+  const int bh = static_cast<int>(blockIdx.x) / n_ctiles;
+  const int ct = n_ctiles - 1 - static_cast<int>(blockIdx.x) % n_ctiles;
+  const int m0 = ct * 2 * kTileRows;
   const int n_ntiles = (S + kTileRows - 1) / kTileRows;
-  const int n_kv = causal ? min(mt + 1, n_ntiles) : n_ntiles;
+  // Key tiles per query tile: tile A (index 2 ct) and tile B (2 ct + 1).
+  const int n_kv_a = causal ? min(2 * ct + 1, n_ntiles) : n_ntiles;
+  const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
 
   uint8_t* sQ = smem + C::kQOff;
   uint8_t* sK = smem + C::kKOff;
@@ -132,10 +155,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* k_empty = k_full + C::kStages;
   uint64_t* v_full = k_empty + C::kStages;
   uint64_t* v_empty = v_full + C::kStages;
-  uint64_t* s_full = v_empty + C::kStages;
-  uint64_t* p_ready = s_full + 2;
-  uint64_t* o_done = p_ready + 2;
-  uint64_t* o_final = o_done + 1;
+  uint64_t* s_full = v_empty + C::kStages;  // [2]
+  uint64_t* p_ready = s_full + 2;           // [2]
+  uint64_t* o_final = p_ready + 2;          // [2]
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
@@ -149,9 +171,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_ready[i], 4);
+      mbar_init(&o_final[i], 1);
     }
-    mbar_init(o_done, 1);
-    mbar_init(o_final, 1);
     ctl->abort = 0;
     fence_mbarrier_init();
   }
@@ -167,88 +188,113 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
 
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, C::kTileBytes);
+  if (wg == 0) {
+    warpgroup_reg_dec<kFwdRegsCtrl>();
+    if (warp == 0 && lane == 0) {
+      // ---------------- TMA producer ----------------
+      mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
 #pragma unroll
-      for (int b = 0; b < D / 64; ++b) tma_load_3d(sQ + b * kBlockBytes, &tm_q, q_full, b * 64, m0, bh);
-      for (int j = 0; j < n_kv; ++j) {
+      for (int x = 0; x < 2; ++x)
+#pragma unroll
+        for (int b = 0; b < D / 64; ++b)
+          tma_load_3d(sQ + x * C::kTileBytes + b * kBlockBytes, &tm_q, q_full, b * 64, m0 + x * kTileRows, bh);
+      for (int j = 0; j < n_kv_b; ++j) {
         const int st = j % C::kStages;
         const uint32_t ph = (j / C::kStages) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, ctl, timeout_ns, status, 1)) break;
         mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
-        uint8_t* kdst = sK + st * C::kTileBytes;
 #pragma unroll
         for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(kdst + b * kBlockBytes, &tm_k, &k_full[st], b * 64, j * kTileRows, bh);
+          tma_load_3d(sK + st * C::kTileBytes + b * kBlockBytes, &tm_k, &k_full[st], b * 64, j * kTileRows, bh);
         if (!mbar_wait(&v_empty[st], ph ^ 1, ctl, timeout_ns, status, 2)) break;
         mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
-        uint8_t* vdst = sV + st * C::kTileBytes;
 #pragma unroll
         for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(vdst + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
+          tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
       }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    } else if (warp == 1 && lane == 0) {
+      // ---------------- MMA issuer ----------------
       const uint32_t idesc_qk = idesc_f16(kBf16 ? 1u : 0u, 128, 128, 0, 0);
       const uint32_t idesc_pv = idesc_f16(kBf16 ? 1u : 0u, 128, D, 0, 1);
       const uint32_t sQa = smem_u32(sQ);
       const uint32_t sKa = smem_u32(sK);
       const uint32_t sVa = smem_u32(sV);
-      bool ok = mbar_wait(q_full, 0, ctl, timeout_ns, status, 3);
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(&p_ready[i & 1], (i >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
-        const int st = i % C::kStages;
-        if (!mbar_wait(&v_full[st], (i / C::kStages) & 1, ctl, timeout_ns, status, 5)) return false;
-        tc_fence_after();
-        const uint32_t p_col = tmem + C::kColS0 + 128u * (i & 1);
-        const uint32_t v_tile = sVa + st * C::kTileBytes;
-#pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk)
-          umma_ts(tmem + C::kColO, p_col + kk * 8, sdesc_mnmajor(v_tile, kTileRows, kk * 16), idesc_pv,
-                  (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&v_empty[st]);
-        umma_commit(o_done);
-        return true;
-      };
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % C::kStages;
-        if (!mbar_wait(&k_full[st], (j / C::kStages) & 1, ctl, timeout_ns, status, 6)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t s_col = tmem + C::kColS0 + 128u * (j & 1);
-        const uint32_t k_tile = sKa + st * C::kTileBytes;
+      auto issue_s = [&](int x, int j) {
+        const uint32_t k_tile = sKa + (j % C::kStages) * C::kTileBytes;
+        const uint32_t q_tile = sQa + x * C::kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(s_col, sdesc_kmajor(sQa, kTileRows, kk * 16), sdesc_kmajor(k_tile, kTileRows, kk * 16),
-                  idesc_qk, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[j & 1]);
-        umma_commit(&k_empty[st]);
-        if (j >= 1) ok = issue_pv(j - 1);
+          umma_ss(tmem + C::kColS0 + 128u * x, sdesc_kmajor(q_tile, kTileRows, kk * 16),
+                  sdesc_kmajor(k_tile, kTileRows, kk * 16), idesc_qk, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t v_tile = sVa + (j % C::kStages) * C::kTileBytes;
+        const uint32_t p_col = tmem + C::kColS0 + 128u * x;
+#pragma unroll
+        for (int kk = 0; kk < kTileRows / 16; ++kk)
+          umma_ts(tmem + C::kColO0 + D * x, p_col + kk * 8, sdesc_mnmajor(v_tile, kTileRows, kk * 16), idesc_pv,
+                  (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, ctl, timeout_ns, status, 3);
+      if (ok) ok = mbar_wait(&k_full[0], 0, ctl, timeout_ns, status, 4);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
       }
-      if (ok) ok = issue_pv(n_kv - 1);
-      if (ok) umma_commit(o_final);
+      for (int j = 0; ok && j < n_kv_b; ++j) {
+        const int st = j % C::kStages;
+        const uint32_t ph = (j / C::kStages) & 1;
+        const int j1 = j + 1;
+        const int st1 = j1 % C::kStages;
+        const uint32_t ph1 = (j1 / C::kStages) & 1;
+        bool v_ready = false, k_ready = false;
+        if (j < n_kv_a) {
+          if (!(ok = mbar_wait(&p_ready[0], j & 1, ctl, timeout_ns, status, 5))) break;
+          if (!(ok = mbar_wait(&v_full[st], ph, ctl, timeout_ns, status, 6))) break;
+          v_ready = true;
+          tc_fence_after();
+          issue_pv(0, j);
+          if (j1 < n_kv_a) {
+            if (!(ok = mbar_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
+            k_ready = true;
+            issue_s(0, j1);
+          } else {
+            umma_commit(&o_final[0]);
+          }
+        }
+        if (!(ok = mbar_wait(&p_ready[1], j & 1, ctl, timeout_ns, status, 8))) break;
+        if (!v_ready && !(ok = mbar_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&v_empty[st]);
+        if (j1 < n_kv_b) {
+          if (!k_ready && !(ok = mbar_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
+          issue_s(1, j1);
+          umma_commit(&k_empty[st1]);
+        } else {
+          umma_commit(&o_final[1]);
+        }
+      }
     }
   } else {
-    // ---------------- softmax / correction / epilogue ----------------
+    warpgroup_reg_inc<kFwdRegsSoftmax>();
+    // ---------------- softmax / correction / epilogue of tile x ----------------
+    const int x = wg - 1;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
-    const int row_g = m0 + r;
+    const int row_g = m0 + x * kTileRows + r;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
+    const uint32_t s_addr = t_lane + C::kColS0 + 128u * x;
+    const uint32_t o_addr = t_lane + C::kColO0 + D * x;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      if (!warp_wait(&s_full[j & 1], (j >> 1) & 1, ctl, timeout_ns, status, 7)) {
-        ok = false;
-        break;
-      }
+    const int n_kv_x = (x == 0) ? n_kv_a : n_kv_b;
+    for (int j = 0; j < n_kv_x; ++j) {
+      if (!(ok = warp_wait(&s_full[x], j & 1, ctl, timeout_ns, status, 11))) break;
       tc_fence_after();
-      const uint32_t s_addr = t_lane + C::kColS0 + 128u * (j & 1);
       uint32_t s[4][32];
 #pragma unroll
       for (int b = 0; b < 4; ++b) tmem_ld32(s_addr + b * 32, s[b]);
@@ -260,47 +306,38 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (causal) lim = min(lim, row_g - n0 + 1);
       float alpha;
       bool need;
-      uint32_t pk[2][32];
-      if (__any_sync(0xffffffffu, lim < kTileRows)) {
-        softmax_tile<D, kBf16, true>(s, lim, scale_log2, m_run, l_run, alpha, need, pk);
-      } else {
-        softmax_tile<D, kBf16, false>(s, lim, scale_log2, m_run, l_run, alpha, need, pk);
-      }
-      tmem_st32(s_addr, pk[0]);
-      tmem_st32(s_addr + 32, pk[1]);
-      if (j >= 1) {
-        // P.V of the previous tile must be finished before O is touched.
-        if (!warp_wait(o_done, (j - 1) & 1, ctl, timeout_ns, status, 8)) {
-          ok = false;
-          break;
-        }
-        if (__any_sync(0xffffffffu, need)) {
-          tc_fence_after();
+      if (__any_sync(0xffffffffu, lim < kTileRows))
+        softmax_tile<kBf16, true>(s, lim, scale_log2, m_run, l_run, alpha, need, s_addr);
+      else
+        softmax_tile<kBf16, false>(s, lim, scale_log2, m_run, l_run, alpha, need, s_addr);
+      // S_x(j) completing implies P_x(j-1).V has completed, so O_x can be
+      // rescaled here, before P_x(j) is released to the MMA warp.
+      if (j >= 1 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
-          for (int cb = 0; cb < D / 32; ++cb) {
-            uint32_t o[32];
-            tmem_ld32(t_lane + C::kColO + cb * 32, o);
-            tmem_wait_ld();
-            reg_fence(o);
+        for (int cb = 0; cb < D / 32; ++cb) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + cb * 32, o);
+          tmem_wait_ld();
+          reg_fence(o);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(t_lane + C::kColO + cb * 32, o);
-          }
+          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+          tmem_st32(o_addr + cb * 32, o);
         }
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[j & 1]);
+      if (lane == 0) mbar_arrive(&p_ready[x]);
     }
-    if (ok) ok = warp_wait(o_final, 0, ctl, timeout_ns, status, 9);
+    uint8_t* stage = sQ + x * C::kTileBytes;  // Q_x is dead once O_x is final
+    if (ok) ok = warp_wait(&o_final[x], 0, ctl, timeout_ns, status, 12);
     if (ok) {
       tc_fence_after();
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
 #pragma unroll
       for (int cb = 0; cb < D / 32; ++cb) {
         uint32_t o[32];
-        tmem_ld32(t_lane + C::kColO + cb * 32, o);
+        tmem_ld32(o_addr + cb * 32, o);
         tmem_wait_ld();
         reg_fence(o);
 #pragma unroll
@@ -310,16 +347,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           w.y = pack2<kBf16>(__uint_as_float(o[ch * 8 + 2]) * inv_l, __uint_as_float(o[ch * 8 + 3]) * inv_l);
           w.z = pack2<kBf16>(__uint_as_float(o[ch * 8 + 4]) * inv_l, __uint_as_float(o[ch * 8 + 5]) * inv_l);
           w.w = pack2<kBf16>(__uint_as_float(o[ch * 8 + 6]) * inv_l, __uint_as_float(o[ch * 8 + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(sQ + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
+          *reinterpret_cast<uint4*>(stage + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
         }
       }
       fence_proxy_async_smem();
     }
-    // Every softmax warp reaches this barrier exactly once, aborted or not.
-    named_barrier_sync(1, 128);
-    if (warp == 2 && lane == 0 && !ctl->abort) {
+    // Every warp of the warpgroup reaches this barrier exactly once.
+    named_barrier_sync(1 + x, 128);
+    // (Tile B of a short sequence may lie wholly past S: nothing to store.)
+    if (q4 == 0 && lane == 0 && !ctl->abort && m0 + x * kTileRows < S) {
 #pragma unroll
-      for (int b = 0; b < D / 64; ++b) tma_store_3d(&tm_o, sQ + b * kBlockBytes, b * 64, m0, bh);
+      for (int b = 0; b < D / 64; ++b)
+        tma_store_3d(&tm_o, stage + b * kBlockBytes, b * 64, m0 + x * kTileRows, bh);
       tma_store_commit();
       tma_store_wait_read_all();
     }
@@ -339,21 +378,27 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 template <int D, bool kBf16>
 int launch_fwd_t(const FwdArgs& a) {
   using C = FwdCfg<D>;
+  static_assert(C::kSmemBytes <= 232448, "forward shared memory exceeds the sm_100 limit");
   auto kern = attn_fwd_kernel<D, kBf16>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
+    // The setmaxnreg split inside the kernel assumes exactly kFwdLaunchRegs
+    // registers per thread at launch; refuse to run a build that differs.
+    cudaFuncAttributes attr;
+    if (cudaFuncGetAttributes(&attr, kern) != cudaSuccess || attr.numRegs != kFwdLaunchRegs)
+      return kErrLaunch;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
         cudaSuccess)
       return kErrLaunch;
     attr_set[dev] = true;
   }
-  const int n_mtiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
-  const long long grid = static_cast<long long>(n_mtiles) * a.BH;
+  const int n_ctiles = static_cast<int>((a.S + 2 * kTileRows - 1) / (2 * kTileRows));
+  const long long grid = static_cast<long long>(n_ctiles) * a.BH;
   kern<<<static_cast<unsigned>(grid), kFwdThreads, C::kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), static_cast<int>(a.BH),
-      n_mtiles, a.causal, a.scale_log2, a.timeout_ns, a.status);
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), static_cast<int>(a.BH), n_ctiles,
+      a.causal, a.scale_log2, a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
