@@ -40,6 +40,11 @@ CONFIGS = {
     "c4": (1, 32, 16384, 128, torch.bfloat16, True, 1.5),
 }
 L2_FLUSH_BYTES = 256 << 20
+# DRAM bytes (read + write) per (batch, head) slab of the C3 shape for one
+# launch of the fused backward kernel, from ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) on 64 slabs (profiles/attn_kernels_c3_bh64.md):
+# 631.3 MB / 64.  Traffic grows in proportion to the slab count.
+BWD_DRAM_BYTES_PER_SLAB_C3 = 631.26e6 / 64
 THROTTLE_REASONS = {
     0x1: "gpu_idle",
     0x2: "applications_clocks_setting",
@@ -298,7 +303,10 @@ def run_ours(args: argparse.Namespace) -> None:
                 "frac": round(achieved / peaks["bf16_tflops"], 4),
                 "frac_of_sustained": round(achieved / peaks["bf16_tflops_sustained"], 4),
                 "peak_source": f"{peaks['source']} bf16 burst (MEASURED_PEAKS.json)",
-                "traffic": args.traffic_bytes,
+                "traffic": args.traffic_bytes if args.traffic_bytes is not None else (
+                    round(BWD_DRAM_BYTES_PER_SLAB_C3 * slab) if (args.config == "c3" and dom == "attn_bwd_fused")
+                    else None),
+                "traffic_source": "ncu dram bytes of one 64-slab launch scaled by slabs/rank",
             },
             "gpu_launches": 4 * steps,
             "gpu_launches_note": "per rank: fwd, bwd_pre, bwd_fused, dq_convert per step",
