@@ -123,8 +123,8 @@ template <int D, bool kBf16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    float* __restrict__ lse, int S, int BH, int n_ctiles, int causal, float scale_log2,
-                    unsigned long long timeout_ns, int* status) {
+                    float* __restrict__ lse, int S, int BH, int n_ctiles, int causal, int lpt_order,
+                    float scale_log2, unsigned long long timeout_ns, int* status) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -134,12 +134,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int wg = warp >> 2;
-  // Head-major order: the query-tile pairs of one (batch, head) are adjacent
-  // in the grid, so the CTAs resident at any time share a few heads' K/V in
-  // L2.  Within a head the heaviest pairs (largest index under a causal
-  // mask) launch first.
-  const int bh = static_cast<int>(blockIdx.x) / n_ctiles;
-  const int ct = n_ctiles - 1 - static_cast<int>(blockIdx.x) % n_ctiles;
+  // Grid order.  Head-major (default): the query-tile pairs of one
+  // (batch, head) are adjacent, so the CTAs resident at any time share a few
+  // heads' K/V in L2; within a head the heaviest pairs (largest index under
+  // a causal mask) launch first.  Heaviest-first across all heads
+  // (lpt_order, chosen by the launcher when every head's K/V fits in L2
+  // together): the longest pairs of every head start in the first waves and
+  // the short ones fill the tail.
+  const int bh = lpt_order ? static_cast<int>(blockIdx.x) % BH : static_cast<int>(blockIdx.x) / n_ctiles;
+  const int ct = n_ctiles - 1 - (lpt_order ? static_cast<int>(blockIdx.x) / BH : static_cast<int>(blockIdx.x) % n_ctiles);
   const int m0 = ct * 2 * kTileRows;
   const int n_ntiles = (S + kTileRows - 1) / kTileRows;
   // Key tiles per query tile: tile A (index 2 ct) and tile B (2 ct + 1).
@@ -396,9 +399,13 @@ int launch_fwd_t(const FwdArgs& a) {
   }
   const int n_ctiles = static_cast<int>((a.S + 2 * kTileRows - 1) / (2 * kTileRows));
   const long long grid = static_cast<long long>(n_ctiles) * a.BH;
+  // Heaviest-first order only pays when it cannot thrash L2: K and V of all
+  // heads together must stay well inside the 126 MB L2.
+  const double kv_bytes = 2.0 * static_cast<double>(a.BH) * static_cast<double>(a.S) * D * 2.0;
+  const int lpt_order = (a.causal && kv_bytes <= 80.0e6) ? 1 : 0;
   kern<<<static_cast<unsigned>(grid), kFwdThreads, C::kSmemBytes, a.stream>>>(
       *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), static_cast<int>(a.BH), n_ctiles,
-      a.causal, a.scale_log2, a.timeout_ns, a.status);
+      a.causal, lpt_order, a.scale_log2, a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
