@@ -19,9 +19,10 @@
 // and walks 128-query steps.  The transposed products are computed directly
 // (S^T = K Q^T, dP^T = V dO^T) so TMEM lane n holds key n.  16 warps in four
 // warpgroups, registers rebalanced with setmaxnreg:
-//   WG0  warp 0   producer: TMA for K, V, Q_i (2 stages), dO_i (1 stage);
-//                 plain loads of LSE/delta
-//        warp 1   TMEM allocator and single-thread tcgen05.mma issuer
+//   WG0  warp 0   producer: TMA for K, V, dO_i (1 stage); plain loads of
+//                 LSE/delta
+//        warp 1   TMEM allocator and tcgen05.mma issuer (the warp runs the
+//                 loop converged, one elected lane issues)
 //        warp 2   issues the TMA reduce-add of each staged dQ tile
 //        warp 3   producer of the Q tiles
 //   WG1  warps 4..7   "dQ warps": thread m owns query m of the step; copy dQ
@@ -281,75 +282,105 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     } else if (warp == 1) {
       // ---------------- MMA issuer ----------------
-      if (lane == 0) {
-        const uint32_t fmt = kBf16 ? 1u : 0u;
-        const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
-        const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
-        const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
-        const uint32_t sKa = smem_u32(sK), sVa = smem_u32(sV), sDSa = smem_u32(sDS);
-        const uint32_t sDOa = smem_u32(sDO);
-        auto issue_s = [&](int it) -> bool {
-          const int st = it & 1;
-          if (!mbar_wait(&q_full[st], (it >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
-          tc_fence_after();
-          const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
+      // The whole warp runs the loop (waits included) so that addresses and
+      // descriptors stay warp-uniform; one elected lane issues each
+      // tcgen05.mma / commit.  Descriptors are precomputed low words plus
+      // compile-time offsets (one add per operand per MMA).
+      const bool leader = elect_one();
+      const uint32_t fmt = kBf16 ? 1u : 0u;
+      const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
+      const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
+      const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
+      const uint32_t k_lo = sdesc_lo_kmajor(smem_u32(sK));
+      const uint32_t k_mn_lo = sdesc_lo_mnmajor(smem_u32(sK), kTileRows);
+      const uint32_t v_lo = sdesc_lo_kmajor(smem_u32(sV));
+      const uint32_t ds_lo = sdesc_lo_kmajor(smem_u32(sDS));
+      const uint32_t ds_mn_lo = sdesc_lo_mnmajor(smem_u32(sDS), kTileRows);
+      const uint32_t do_lo = sdesc_lo_kmajor(smem_u32(sDO));
+      const uint32_t do_mn_lo = sdesc_lo_mnmajor(smem_u32(sDO), kTileRows);
+      const uint32_t q_lo0 = sdesc_lo_kmajor(smem_u32(sQ));
+      const uint32_t q_mn_lo0 = sdesc_lo_mnmajor(smem_u32(sQ), kTileRows);
+      constexpr uint32_t kTileLo = C::kTileBytes >> 4;  // low-word step between Q stages
+      auto commit = [&](uint64_t* bar) {
+        if (leader) umma_commit(bar);
+        __syncwarp();
+      };
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        if (!warp_wait(&q_full[st], (it >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
+        tc_fence_after();
+        const uint32_t q_lo = q_lo0 + st * kTileLo;
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(tmem + C::kColS, sdesc_kmajor(sKa, kTileRows, kk * 16),
-                    sdesc_kmajor(sQa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
+            umma_ss_w(tmem + C::kColS, k_lo + kmajor_koff(kTileRows, kk * 16), q_lo + kmajor_koff(kTileRows, kk * 16),
+                      idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(s_full);
-          return true;
-        };
-        auto issue_dp = [&](int it) -> bool {
-          if (!mbar_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
-          if (C::kDqAliased && it > 0) {
-            if (!mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
-          }
-          tc_fence_after();
+        }
+        __syncwarp();
+        return true;
+      };
+      auto issue_dp = [&](int it) -> bool {
+        if (!warp_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
+        if (C::kDqAliased && it > 0) {
+          if (!warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
+        }
+        tc_fence_after();
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss(tmem + C::kColDP, sdesc_kmajor(sVa, kTileRows, kk * 16),
-                    sdesc_kmajor(sDOa, kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
+            umma_ss_w(tmem + C::kColDP, v_lo + kmajor_koff(kTileRows, kk * 16), do_lo + kmajor_koff(kTileRows, kk * 16),
+                      idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(dp_full);
-          return true;
-        };
-        bool ok = mbar_wait(kv_full, 0, ctl, timeout_ns, status, 7);
-        if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
-        for (int it = 0; ok && it < n_steps; ++it) {
-          const int st = it & 1;
-          const uint32_t sQa = smem_u32(sQ + st * C::kTileBytes);
-          // dV += P^T dO.  P^T of queries 64h..64h+63 sits packed in the
-          // first 32 columns of warpgroup h's 64 S columns.
-          if (!(ok = mbar_wait(p_ready, it & 1, ctl, timeout_ns, status, 8))) break;
-          tc_fence_after();
+        }
+        __syncwarp();
+        return true;
+      };
+      bool ok = warp_wait(kv_full, 0, ctl, timeout_ns, status, 7);
+      if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
+      for (int it = 0; ok && it < n_steps; ++it) {
+        const int st = it & 1;
+        const uint32_t q_mn_lo = q_mn_lo0 + st * kTileLo;
+        // dV += P^T dO.  P^T of queries 64h..64h+63 sits packed in the
+        // first 32 columns of warpgroup h's 64 S columns.
+        if (!(ok = warp_wait(p_ready, it & 1, ctl, timeout_ns, status, 8))) break;
+        tc_fence_after();
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_ts(tmem + C::kColDV, tmem + C::kColS + (kk >> 2) * 64 + (kk & 3) * 8,
-                    sdesc_mnmajor(sDOa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_ts_w(tmem + C::kColDV, tmem + C::kColS + (kk >> 2) * 64 + (kk & 3) * 8,
+                      do_mn_lo + mnmajor_koff(kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
           umma_commit(do_empty);
-          if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
-          // dK += dS^T Q  (dS^T in smem from the dS warps)
-          if (!(ok = mbar_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
-          tc_fence_after();
+        }
+        __syncwarp();
+        if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
+        // dK += dS^T Q  (dS^T in smem from the dS warps)
+        if (!(ok = warp_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
+        tc_fence_after();
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_ss(tmem + C::kColDK, sdesc_kmajor(sDSa, kTileRows, kk * 16),
-                    sdesc_mnmajor(sQa, kTileRows, kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_ss_w(tmem + C::kColDK, ds_lo + kmajor_koff(kTileRows, kk * 16), q_mn_lo + mnmajor_koff(kk * 16),
+                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
           umma_commit(&q_empty[st]);
-          // dQ = dS K
-          if (!C::kDqAliased && it > 0) {
-            if (!(ok = mbar_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
-          }
+        }
+        __syncwarp();
+        // dQ = dS K
+        if (!C::kDqAliased && it > 0) {
+          if (!(ok = warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
+        }
+        if (leader) {
 #pragma unroll
           for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_ss(tmem + C::kColDQ, sdesc_mnmajor(sDSa, kTileRows, kk * 16),
-                    sdesc_mnmajor(sKa, kTileRows, kk * 16), idesc_dq, kk > 0 ? 1u : 0u);
+            umma_ss_w(tmem + C::kColDQ, ds_mn_lo + mnmajor_koff(kk * 16), k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
+                      kk > 0 ? 1u : 0u);
           umma_commit(dq_full);
           umma_commit(ds_empty);
-          if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
         }
-        if (ok) umma_commit(dkdv_done);
+        __syncwarp();
+        if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
       }
+      if (ok) commit(dkdv_done);
     } else if (warp == 2) {
       // ---------------- dQ reduce issuer ----------------
       bool ok = true;

@@ -16,7 +16,8 @@
 // three warpgroups, registers rebalanced with setmaxnreg:
 //   WG0  warp 0   TMA producer (Q_A and Q_B once, then K and V tiles
 //                 through two rings)
-//        warp 1   TMEM allocator and single-thread tcgen05.mma issuer
+//        warp 1   TMEM allocator and tcgen05.mma issuer (the warp runs the
+//                 loop converged, one elected lane issues)
 //   WG1  warps 4..7   softmax of tile A: thread t owns query row t (TMEM
 //                     lane t); also rescales O_A when its running maximum
 //                     moves, and runs tile A's epilogue
@@ -73,49 +74,87 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaCon
   return __all_sync(0xffffffffu, ok);
 }
 
-// Online-softmax step for one row and one 128-key tile held in s[4][32]:
+// Of every 8 column pairs of an unmasked tile, this many take their exp2 on
+// the FMA pipe (exp2_fma) and the rest on the MUFU, which alone would bound a
+// tile at 1024 cycles (16384 exponentials at 16 per clock).
+constexpr int kEmuPairsPer8 = 0;
+
+template <bool kMasked>
+__device__ __forceinline__ void max_chunk(uint32_t (&s)[32], int col0, int lim, float (&mx)[8]) {
+#pragma unroll
+  for (int c = 0; c < 32; c += 2) {
+    float v0 = __uint_as_float(s[c]), v1 = __uint_as_float(s[c + 1]);
+    if constexpr (kMasked) {
+      if (col0 + c >= lim) {
+        v0 = -INFINITY;
+        s[c] = __float_as_uint(v0);
+      }
+      if (col0 + c + 1 >= lim) {
+        v1 = -INFINITY;
+        s[c + 1] = __float_as_uint(v1);
+      }
+    }
+    mx[(c >> 1) & 7] = fmax3(mx[(c >> 1) & 7], v0, v1);
+  }
+}
+
+// Online-softmax step for one row and one 128-key tile of S at s_addr (TMEM):
+// loads S (two halves, the second overlapping the first half's maximum),
 // updates the running maximum / sum, returns the rescale factor of the
 // previous accumulator (alpha) and whether the maximum moved (need), and
 // writes P (16-bit pairs) over the first 64 TMEM columns at s_addr.
 template <bool kBf16, bool kMasked>
-__device__ __forceinline__ void softmax_tile(uint32_t (&s)[4][32], int lim, float scale_log2,
-                                             float& m_run, float& l_run, float& alpha, bool& need,
-                                             uint32_t s_addr) {
-  float mx = -INFINITY;
+__device__ __forceinline__ void softmax_tile(uint32_t s_addr, int lim, float scale_log2, float& m_run,
+                                             float& l_run, float& alpha, bool& need) {
+  uint32_t s[4][32];
+  tmem_ld32(s_addr, s[0]);
+  tmem_ld32(s_addr + 32, s[1]);
+  tmem_wait_ld();
+  reg_fence(s[0]);
+  reg_fence(s[1]);
+  tmem_ld32(s_addr + 64, s[2]);
+  tmem_ld32(s_addr + 96, s[3]);
+  float mx[8];
 #pragma unroll
-  for (int b = 0; b < 4; ++b) {
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      float v = __uint_as_float(s[b][c]);
-      if constexpr (kMasked) {
-        if (b * 32 + c >= lim) {
-          v = -INFINITY;
-          s[b][c] = __float_as_uint(v);
-        }
-      }
-      mx = fmaxf(mx, v);
-    }
-  }
-  const float m_new = fmaxf(m_run, mx * scale_log2);
+  for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+  max_chunk<kMasked>(s[0], 0, lim, mx);
+  max_chunk<kMasked>(s[1], 32, lim, mx);
+  tmem_wait_ld();
+  reg_fence(s[2]);
+  reg_fence(s[3]);
+  max_chunk<kMasked>(s[2], 64, lim, mx);
+  max_chunk<kMasked>(s[3], 96, lim, mx);
+  const float mxa = fmax3(mx[0], mx[1], mx[2]), mxb = fmax3(mx[3], mx[4], mx[5]);
+  const float m_tile = fmax3(mxa, mxb, fmaxf(mx[6], mx[7]));
+  const float m_new = fmaxf(m_run, m_tile * scale_log2);
   need = m_new > m_run + kRescaleThreshold;
   const float m_use = need ? m_new : m_run;
   alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_use);
   const float ms = (m_use == -INFINITY) ? 0.0f : m_use;
-  float sum0 = 0.0f, sum1 = 0.0f;
+  float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     uint32_t pk[16];
 #pragma unroll
     for (int c = 0; c < 32; c += 2) {
-      const float p0 = ex2(fmaf(__uint_as_float(s[b][c]), scale_log2, -ms));
-      const float p1 = ex2(fmaf(__uint_as_float(s[b][c + 1]), scale_log2, -ms));
-      sum0 += p0;
-      sum1 += p1;
+      const float x0 = fmaf(__uint_as_float(s[b][c]), scale_log2, -ms);
+      const float x1 = fmaf(__uint_as_float(s[b][c + 1]), scale_log2, -ms);
+      float p0, p1;
+      // Masked tiles keep every exponential on the MUFU so that masked
+      // entries are exactly zero.
+      if (!kMasked && ((c >> 1) & 7) >= 8 - kEmuPairsPer8) {
+        p0 = exp2_fma(x0);
+        p1 = exp2_fma(x1);
+      } else {
+        p0 = ex2(x0);
+        p1 = ex2(x1);
+      }
+      sum[(c >> 1) & 3] += p0 + p1;
       pk[c >> 1] = pack2<kBf16>(p0, p1);
     }
     tmem_st16(s_addr + b * 16, pk);
   }
-  l_run = l_run * alpha + (sum0 + sum1);
+  l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
   m_run = m_use;
 }
 
@@ -215,37 +254,55 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int b = 0; b < D / 64; ++b)
           tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
       }
-    } else if (warp == 1 && lane == 0) {
+    } else if (warp == 1) {
       // ---------------- MMA issuer ----------------
+      // The whole warp runs the loop (waits included) so that addresses and
+      // descriptors stay warp-uniform; one elected lane issues each
+      // tcgen05.mma / commit.  Descriptors are precomputed low words plus
+      // compile-time offsets (one add per operand per MMA).
+      const bool leader = elect_one();
       const uint32_t idesc_qk = idesc_f16(kBf16 ? 1u : 0u, 128, 128, 0, 0);
       const uint32_t idesc_pv = idesc_f16(kBf16 ? 1u : 0u, 128, D, 0, 1);
-      const uint32_t sQa = smem_u32(sQ);
-      const uint32_t sKa = smem_u32(sK);
-      const uint32_t sVa = smem_u32(sV);
+      const uint32_t q_lo0 = sdesc_lo_kmajor(smem_u32(sQ));
+      const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(sK));
+      const uint32_t v_lo0 = sdesc_lo_mnmajor(smem_u32(sV), kTileRows);
+      constexpr uint32_t kTileLo = C::kTileBytes >> 4;  // low-word step between tiles
       auto issue_s = [&](int x, int j) {
-        const uint32_t k_tile = sKa + (j % C::kStages) * C::kTileBytes;
-        const uint32_t q_tile = sQa + x * C::kTileBytes;
+        const uint32_t q_lo = q_lo0 + x * kTileLo;
+        const uint32_t k_lo = k_lo0 + (j % C::kStages) * kTileLo;
+        const uint32_t d = tmem + C::kColS0 + 128u * x;
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_ss(tmem + C::kColS0 + 128u * x, sdesc_kmajor(q_tile, kTileRows, kk * 16),
-                  sdesc_kmajor(k_tile, kTileRows, kk * 16), idesc_qk, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[x]);
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_ss_w(d, q_lo + kmajor_koff(kTileRows, kk * 16), k_lo + kmajor_koff(kTileRows, kk * 16), idesc_qk,
+                      kk > 0 ? 1u : 0u);
+          umma_commit(&s_full[x]);
+        }
+        __syncwarp();
       };
       auto issue_pv = [&](int x, int j) {
-        const uint32_t v_tile = sVa + (j % C::kStages) * C::kTileBytes;
+        const uint32_t v_lo = v_lo0 + (j % C::kStages) * kTileLo;
         const uint32_t p_col = tmem + C::kColS0 + 128u * x;
+        const uint32_t d = tmem + C::kColO0 + D * x;
+        const uint32_t acc0 = j > 0 ? 1u : 0u;
+        if (leader) {
 #pragma unroll
-        for (int kk = 0; kk < kTileRows / 16; ++kk)
-          umma_ts(tmem + C::kColO0 + D * x, p_col + kk * 8, sdesc_mnmajor(v_tile, kTileRows, kk * 16), idesc_pv,
-                  (j > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ts_w(d, p_col + kk * 8, v_lo + mnmajor_koff(kk * 16), idesc_pv, kk > 0 ? 1u : acc0);
+        }
+        __syncwarp();
       };
-      bool ok = mbar_wait(q_full, 0, ctl, timeout_ns, status, 3);
-      if (ok) ok = mbar_wait(&k_full[0], 0, ctl, timeout_ns, status, 4);
+      auto commit = [&](uint64_t* bar) {
+        if (leader) umma_commit(bar);
+        __syncwarp();
+      };
+      bool ok = warp_wait(q_full, 0, ctl, timeout_ns, status, 3);
+      if (ok) ok = warp_wait(&k_full[0], 0, ctl, timeout_ns, status, 4);
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
         issue_s(1, 0);
-        umma_commit(&k_empty[0]);
+        commit(&k_empty[0]);
       }
       for (int j = 0; ok && j < n_kv_b; ++j) {
         const int st = j % C::kStages;
@@ -255,30 +312,30 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const uint32_t ph1 = (j1 / C::kStages) & 1;
         bool v_ready = false, k_ready = false;
         if (j < n_kv_a) {
-          if (!(ok = mbar_wait(&p_ready[0], j & 1, ctl, timeout_ns, status, 5))) break;
-          if (!(ok = mbar_wait(&v_full[st], ph, ctl, timeout_ns, status, 6))) break;
+          if (!(ok = warp_wait(&p_ready[0], j & 1, ctl, timeout_ns, status, 5))) break;
+          if (!(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 6))) break;
           v_ready = true;
           tc_fence_after();
           issue_pv(0, j);
           if (j1 < n_kv_a) {
-            if (!(ok = mbar_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
+            if (!(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
             k_ready = true;
             issue_s(0, j1);
           } else {
-            umma_commit(&o_final[0]);
+            commit(&o_final[0]);
           }
         }
-        if (!(ok = mbar_wait(&p_ready[1], j & 1, ctl, timeout_ns, status, 8))) break;
-        if (!v_ready && !(ok = mbar_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
+        if (!(ok = warp_wait(&p_ready[1], j & 1, ctl, timeout_ns, status, 8))) break;
+        if (!v_ready && !(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
         tc_fence_after();
         issue_pv(1, j);
-        umma_commit(&v_empty[st]);
+        commit(&v_empty[st]);
         if (j1 < n_kv_b) {
-          if (!k_ready && !(ok = mbar_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
+          if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
           issue_s(1, j1);
-          umma_commit(&k_empty[st1]);
+          commit(&k_empty[st1]);
         } else {
-          umma_commit(&o_final[1]);
+          commit(&o_final[1]);
         }
       }
     }
@@ -298,21 +355,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     for (int j = 0; j < n_kv_x; ++j) {
       if (!(ok = warp_wait(&s_full[x], j & 1, ctl, timeout_ns, status, 11))) break;
       tc_fence_after();
-      uint32_t s[4][32];
-#pragma unroll
-      for (int b = 0; b < 4; ++b) tmem_ld32(s_addr + b * 32, s[b]);
-      tmem_wait_ld();
-#pragma unroll
-      for (int b = 0; b < 4; ++b) reg_fence(s[b]);
       const int n0 = j * kTileRows;
       int lim = S - n0;
       if (causal) lim = min(lim, row_g - n0 + 1);
       float alpha;
       bool need;
       if (__any_sync(0xffffffffu, lim < kTileRows))
-        softmax_tile<kBf16, true>(s, lim, scale_log2, m_run, l_run, alpha, need, s_addr);
+        softmax_tile<kBf16, true>(s_addr, lim, scale_log2, m_run, l_run, alpha, need);
       else
-        softmax_tile<kBf16, false>(s, lim, scale_log2, m_run, l_run, alpha, need, s_addr);
+        softmax_tile<kBf16, false>(s_addr, lim, scale_log2, m_run, l_run, alpha, need);
       // S_x(j) completing implies P_x(j-1).V has completed, so O_x can be
       // rescaled here, before P_x(j) is released to the MMA warp.
       if (j >= 1 && __any_sync(0xffffffffu, need)) {

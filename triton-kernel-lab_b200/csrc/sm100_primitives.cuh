@@ -266,6 +266,61 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// The same SW128 descriptors split into two 32-bit words.  The high word
+// (stride byte offset 1024, version 1, SWIZZLE_128B) is the same for every
+// operand here; the low word holds the start address (>> 4) and the leading
+// byte offset.  Within a tile only the start address changes from one MMA
+// to the next, and shared addresses stay below 256 KB, so a per-MMA low word
+// is `base + constant` with no carry into the offset field: the issuing
+// thread spends one add per operand per MMA.
+constexpr uint32_t kSdescHi = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t sdesc_lo_kmajor(uint32_t tile_saddr) {
+  return ((tile_saddr >> 4) & 0x3FFFu) | ((16u >> 4) << 16);
+}
+__device__ __forceinline__ uint32_t sdesc_lo_mnmajor(uint32_t tile_saddr, uint32_t rows) {
+  return ((tile_saddr >> 4) & 0x3FFFu) | (((rows * kSwizzleBytes) >> 4) << 16);
+}
+// Start-address increments (16-byte units) of K element k (a multiple of 16).
+__host__ __device__ constexpr uint32_t kmajor_koff(uint32_t rows, uint32_t k) {
+  return ((k >> 6) * rows * kSwizzleBytes + (k & 63u) * 2u) >> 4;
+}
+__host__ __device__ constexpr uint32_t mnmajor_koff(uint32_t k) { return (k * kSwizzleBytes) >> 4; }
+
+__device__ __forceinline__ void umma_ss_w(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSdescHi)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kSdescHi)
+      : "memory");
+}
+
+// One lane of a converged warp (elect.sync): the lane that issues
+// single-thread tcgen05 operations while the whole warp runs the loop.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive once on `bar` when every tcgen05.mma previously issued by this
 // thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -397,6 +452,35 @@ __device__ __forceinline__ float lg2(float x) {
   float y;
   asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Base-2 exponential on the FMA pipe, for splitting a softmax's exponentials
+// between the MUFU (16 per clock per SM) and the FP32 units.  Method
+// (Cody-Waite style range reduction): x = n + f with n = round(x) taken from
+// the low mantissa bits of x + 1.5*2^23, f in [-1/2, 1/2]; 2^f from a degree-4
+// polynomial fitted here for minimum relative error on [-1/2, 1/2]
+// (Lawson-weighted least squares, max relative error 2.7e-6 measured in fp32
+// Horner form); n is added to the exponent field.  Valid for x <= 127;
+// inputs below -126 are clamped to -126, so they return a value of at most
+// 2^-126 instead of 0 (callers use it only where no element is masked).
+__device__ __forceinline__ float exp2_fma(float x) {
+  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+  x = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(x, kShift);
+  const float n = __fsub_rn(t, kShift);
+  const float f = __fsub_rn(x, n);
+  float p = fmaf(9.570101276e-03f, f, 5.591785908e-02f);
+  p = fmaf(p, f, 2.402474433e-01f);
+  p = fmaf(p, f, 6.931217909e-01f);
+  p = fmaf(p, f, 9.999992847e-01f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
+// Three-input maximum (sm_100 max.f32 with three sources).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Pack two floats into one 32-bit word of 16-bit values, `lo` in bits 0..15
