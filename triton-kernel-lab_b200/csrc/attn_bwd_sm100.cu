@@ -33,8 +33,9 @@
 //                     warpgroup's own S^T columns for the dV MMA.  Phase 2:
 //                     dS^T = P^T (dP^T - delta) to smem for the dK and dQ
 //                     MMAs.  Epilogue: WG2 stores dV, WG3 stores dK.
-// MMA issue order per step i: dV_i, S_{i+1}, dK_i, dQ_i, dP_{i+1}, so the dS
-// warps compute P_{i+1} (the exp2-heavy phase) while dK_i and dQ_i run.
+// MMA issue order per step i: dV_i, S_{i+1}, dQ_i, dK_i, dP_{i+1}, so the dS
+// warps compute P_{i+1} (the exp2-heavy phase) while dQ_i and dK_i run, and
+// the dQ warps drain dQ_i from TMEM while dK_i runs.
 // TMEM columns: dV [0,D) dK [D,2D) S^T/P^T [2D,2D+128) dP^T [2D+128,2D+256);
 // dQ follows dP^T when it fits (D=64) and otherwise (D=128) reuses the dP^T
 // columns, reclaimed by dP_{i+1} only after the dQ warps have read dQ_i.
@@ -354,18 +355,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
         __syncwarp();
         if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
-        // dK += dS^T Q  (dS^T in smem from the dS warps)
+        // dQ = dS K  (dS in smem from the dS warps)
         if (!(ok = warp_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
         tc_fence_after();
-        if (leader) {
-#pragma unroll
-          for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_ss_w(tmem + C::kColDK, ds_lo + kmajor_koff(kTileRows, kk * 16), q_mn_lo + mnmajor_koff(kk * 16),
-                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&q_empty[st]);
-        }
-        __syncwarp();
-        // dQ = dS K
         if (!C::kDqAliased && it > 0) {
           if (!(ok = warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
         }
@@ -375,6 +367,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             umma_ss_w(tmem + C::kColDQ, ds_mn_lo + mnmajor_koff(kk * 16), k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
                       kk > 0 ? 1u : 0u);
           umma_commit(dq_full);
+        }
+        __syncwarp();
+        // dK += dS^T Q; the smem dS tile is free after this one.
+        if (leader) {
+#pragma unroll
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ss_w(tmem + C::kColDK, ds_lo + kmajor_koff(kTileRows, kk * 16), q_mn_lo + mnmajor_koff(kk * 16),
+                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&q_empty[st]);
           umma_commit(ds_empty);
         }
         __syncwarp();
@@ -464,20 +465,28 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const float* lse_s = sLse + lb * 128 + h * 64;
       const float* del_s = sDelta + lb * 128 + h * 64;
       // Phase 1: P^T for this warpgroup's 64 queries -> registers and,
-      // packed to 16 bits, back over the first 32 of its S columns (each
-      // 32-column chunk is read before its packed half is written).
+      // packed to 16 bits, back over the first 32 of its S columns (both
+      // 32-column chunks are read before any packed half is written).
       float p[2][32];
       const bool masked = __any_sync(0xffffffffu, diag || !key_ok);
+      {
+        // Both 32-column loads are in flight together.
+        uint32_t sv[2][32];
+        tmem_ld32(s_cols, sv[0]);
+        tmem_ld32(s_cols + 32, sv[1]);
+        tmem_wait_ld();
+        reg_fence(sv[0]);
+        reg_fence(sv[1]);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          if (masked)
+            probs_chunk<true>(sv[c], lse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
+          else
+            probs_chunk<false>(sv[c], lse_s + c * 32, scale_log2, 0, 0, true, p[c]);
+        }
+      }
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32];
-        tmem_ld32(s_cols + c * 32, sv);
-        tmem_wait_ld();
-        reg_fence(sv);
-        if (masked)
-          probs_chunk<true>(sv, lse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
-        else
-          probs_chunk<false>(sv, lse_s + c * 32, scale_log2, 0, 0, true, p[c]);
         uint32_t pp[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
@@ -493,12 +502,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 14))) break;
       }
       tc_fence_after();
+      uint32_t dpv2[2][32];
+      tmem_ld32(dp_cols, dpv2[0]);
+      tmem_ld32(dp_cols + 32, dpv2[1]);
+      tmem_wait_ld();
+      reg_fence(dpv2[0]);
+      reg_fence(dpv2[1]);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t dpv[32];
-        tmem_ld32(dp_cols + c * 32, dpv);
-        tmem_wait_ld();
-        reg_fence(dpv);
+        const uint32_t (&dpv)[32] = dpv2[c];
         uint32_t dd[16];
         const float4* del4 = reinterpret_cast<const float4*>(del_s + c * 32);
 #pragma unroll
