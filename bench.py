@@ -437,6 +437,91 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_sweep(args: argparse.Namespace) -> None:
+    """C5 sweep: fp16 and bf16, causal and non-causal, D in {64, 128},
+    S in {512, ..., 16384} with B = 16384 / S and H = 16 (seeded N(0,1)
+    inputs).  Forward (with LSE) and backward (preprocess + fused kernel +
+    dQ conversion) are timed separately with CUDA events after an L2 flush;
+    the (batch*head) slabs are split over the ranks as in the main benchmark
+    and the time is the max over ranks.  Rank 0 prints one JSON line per
+    configuration (these lines are not the benchmark's headline line)."""
+    from tklab import _native
+    from tklab.kernels.flash_attention import _NATIVE_DTYPE
+    from tklab.sharding import slab_range
+
+    rank, world, local_rank = _dist_env()
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    lib = _native.load()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    sp = int(stream.cuda_stream)
+    for dtype in (torch.float16, torch.bfloat16):
+        for causal in (False, True):
+            for d in (64, 128):
+                for s in (512, 1024, 2048, 4096, 8192, 16384):
+                    b, h = 16384 // s, 16
+                    start_bh, stop_bh = slab_range(b * h, world, rank)
+                    slab = stop_bh - start_bh
+                    shape = (1, slab, s, d)
+                    q, k, v, do = _make_inputs(shape, dtype, 1.0, seed=args.seed + rank, device=device)
+                    o = torch.empty_like(q)
+                    lse = torch.empty((1, slab, s), dtype=torch.float32, device=device)
+                    delta = torch.empty_like(lse)
+                    acc = torch.empty(shape, dtype=torch.float32, device=device)
+                    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+                    nd = _NATIVE_DTYPE[dtype]
+                    scale = 1.0 / math.sqrt(d)
+
+                    def fwd() -> None:
+                        _native.check(lib.tk_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                                      lse.data_ptr(), 1, slab, s, d, nd, int(causal), scale, sp), "fwd")
+
+                    def bwd() -> None:
+                        _native.check(lib.tk_attn_bwd_pre(o.data_ptr(), do.data_ptr(), delta.data_ptr(),
+                                                          acc.data_ptr(), 1, slab, s, d, nd, sp), "bwd_pre")
+                        _native.check(lib.tk_attn_bwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                                      lse.data_ptr(), delta.data_ptr(), acc.data_ptr(), dq.data_ptr(),
+                                                      dk.data_ptr(), dv.data_ptr(), 1, slab, s, d, nd, int(causal),
+                                                      scale, sp), "bwd")
+
+                    times = {}
+                    for name, fn in (("fwd", fwd), ("bwd", bwd)):
+                        for _ in range(args.warmup):
+                            fn()
+                        samples = []
+                        for _ in range(args.steps):
+                            flush.zero_()
+                            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            e0.record(stream)
+                            fn()
+                            e1.record(stream)
+                            torch.cuda.synchronize(device)
+                            samples.append(e0.elapsed_time(e1))
+                        t = torch.tensor([statistics.median(samples)], dtype=torch.float64, device=device)
+                        if world > 1:
+                            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+                        times[name] = float(t.item())
+                    if rank == 0:
+                        ff, bf = fwd_flops(b, h, s, d, causal), bwd_flops(b, h, s, d, causal)
+                        print(json.dumps({
+                            "sweep": "c5", "dtype": str(dtype).replace("torch.", ""), "causal": causal, "D": d,
+                            "S": s, "B": b, "H": h, "n_gpus": world, "fwd_ms": round(times["fwd"], 4),
+                            "bwd_ms": round(times["bwd"], 4),
+                            "fwd_tflops": round(ff / times["fwd"] / 1e9, 1),
+                            "bwd_tflops": round(bf / times["bwd"] / 1e9, 1),
+                            "bwd_timed": "tk_attn_bwd_pre + tk_attn_bwd (fused kernel + dQ conversion)",
+                            "l2": "flushed before every timed call"}), flush=True)
+                    del q, k, v, do, o, lse, delta, acc, dq, dk, dv
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -453,10 +538,14 @@ def main() -> None:
                         help="(batch*head) slabs per rank instead of the config's (profiling only)")
     parser.add_argument("--traffic-bytes", type=float, default=None,
                         help="ncu dram bytes per launch of the dominant kernel, if captured")
+    parser.add_argument("--sweep", action="store_true",
+                        help="C5 sweep (fwd and bwd per dtype/causal/D/S), one JSON line per configuration")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
-    if args.impl == "reference":
+    if args.sweep:
+        run_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
