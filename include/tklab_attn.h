@@ -62,8 +62,10 @@ extern "C" {
 
 /* Forward attention.  o receives softmax(scale * q k^T) v (causal: key n
  * attends query m only when n <= m).  lse may be NULL; otherwise it
- * receives the base-2 log-sum-exp of every query row.  head_dim must be 64
- * or 128; q, k, v, o must be 16-byte aligned. */
+ * receives the base-2 log-sum-exp of every query row.  head_dim must be a
+ * multiple of 8 from 8 to 128 (widths other than 64 and 128 run the 64- or
+ * 128-column kernel with the missing columns zero-filled on load and clipped
+ * on store); q, k, v, o must be 16-byte aligned. */
 TK_API int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
                 void* stream);
@@ -109,6 +111,29 @@ TK_API int tk_attn_bwd_noalloc(const void* q, const void* k, const void* v, cons
                                const void* d_o, const float* lse, void* dq, void* dk, void* dv,
                                int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                                int dtype, int causal, float scale, void* stream);
+
+/* Deterministic backward: dQ is produced by a query-stationary kernel that
+ * keeps it in tensor memory and adds the key tiles in one fixed order, with
+ * no atomics, so repeated calls give bitwise identical dq; dk and dv come
+ * from the fused kernel with its dQ path compiled out (bitwise identical to
+ * tk_attn_bwd's dk and dv).  No fp32 accumulator, no conversion pass.
+ * Replaces the reference's two backward launches `_attn_bwd_dkdv_kernel` and
+ * `_attn_bwd_dq_kernel` (src/tklab/kernels/flash_attention.py:570-606),
+ * which are deterministic the same way.
+ *   tk_attn_bwd_dkdv          dK, dV from q, k, v, dO, lse and delta
+ *   tk_attn_bwd_dq            dQ (input dtype, scale applied)
+ *   tk_attn_bwd_deterministic delta (tk_attn_bwd_pre without the clear), then
+ *                             both of the above */
+TK_API int tk_attn_bwd_dkdv(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                            const float* delta, void* dk, void* dv, int64_t batch, int64_t heads, int64_t seq,
+                            int64_t head_dim, int dtype, int causal, float scale, void* stream);
+TK_API int tk_attn_bwd_dq(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                          const float* delta, void* dq, int64_t batch, int64_t heads, int64_t seq,
+                          int64_t head_dim, int dtype, int causal, float scale, void* stream);
+TK_API int tk_attn_bwd_deterministic(const void* q, const void* k, const void* v, const void* o,
+                                     const void* d_o, const float* lse, float* delta, void* dq, void* dk,
+                                     void* dv, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                     int dtype, int causal, float scale, void* stream);
 
 /* Bytes of the fp32 dQ accumulator tk_attn_bwd needs (0 on bad sizes). */
 TK_API size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);

@@ -44,7 +44,8 @@ def test_workspace_size_arithmetic() -> None:
     ("kwargs", "status"),
     [
         ({"q": None}, 1),
-        ({"head_dim": 96}, 2),
+        ({"head_dim": 100}, 2),
+        ({"head_dim": 136}, 2),
         ({"head_dim": 256}, 2),
         ({"dtype": 7}, 2),
         ({"seq": 0}, 1),

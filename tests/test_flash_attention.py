@@ -93,3 +93,27 @@ def test_widened_contract_matches_sdpa(
     assert_relative_frobenius(output, reference, max_relative_error=2e-2)
     assert (output.float() - reference).abs().max().item() <= 2e-2
     check_device_status()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("head_dim", [8, 32, 48, 80, 96, 112])
+@pytest.mark.parametrize("causal", [False, True])
+def test_general_head_dim_matches_sdpa(dtype: torch.dtype, head_dim: int, causal: bool) -> None:
+    """Head dims that are not a kernel width (run with the columns past head_dim zero-filled on load
+    and clipped on store) against fp32 SDPA, with the base-2 LSE."""
+    torch.manual_seed(11 * head_dim + int(causal))
+    shape = (2, 3, 333, head_dim)
+    q, k, v = (torch.randn(shape, device="cuda", dtype=dtype) for _ in range(3))
+    output = torch.full_like(q, float("nan"))
+    lse = torch.full(shape[:3], float("nan"), device="cuda")
+    _launch_forward(q, k, v, output, lse, causal=causal, store_lse=True)
+    reference = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
+    assert torch.isfinite(output).all()
+    assert_relative_frobenius(output, reference, max_relative_error=2e-2)
+    assert (output.float() - reference).abs().max().item() <= 2e-2
+    scores = q.float() @ k.float().transpose(-1, -2) / math.sqrt(head_dim)
+    if causal:
+        scores = scores.masked_fill(torch.ones(333, 333, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
+    expected = torch.logsumexp(scores, dim=-1) / math.log(2.0)
+    assert (lse - expected).abs().max().item() <= 1e-3 * max(1.0, expected.abs().max().item())
+    check_device_status()

@@ -97,3 +97,23 @@ def test_widened_backward_matches_manual_algebra(
             continue
         assert_relative_frobenius(grad, reference_grad, max_relative_error=3e-2)
     check_device_status()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("head_dim", [8, 32, 48, 80, 96, 112])
+@pytest.mark.parametrize("causal", [False, True])
+def test_general_head_dim_backward_matches_manual_algebra(dtype: torch.dtype, head_dim: int, causal: bool) -> None:
+    """Gradients for head dims that are not a kernel width (zero-filled loads, clipped stores and
+    dQ reductions past head_dim) against the fp32 algebra."""
+    torch.manual_seed(13 * head_dim + int(causal))
+    q, k, v, do = _inputs(300, dtype=dtype, head_dim=head_dim, heads=3)
+    expected = manual_backward(q, k, v, do, causal=causal)
+    output = (attention_causal if causal else attention_noncausal)(q, k, v)
+    actual = torch.autograd.grad(output, (q, k, v), grad_outputs=do)
+    for name, grad, reference_grad in zip(("dq", "dk", "dv"), actual, expected, strict=True):
+        grad = grad.float().cpu()
+        assert grad.shape == reference_grad.shape, name
+        assert torch.isfinite(grad).all(), name
+        assert (grad - reference_grad).abs().max().item() <= 5e-2, name
+        assert_relative_frobenius(grad, reference_grad, max_relative_error=3e-2)
+    check_device_status()

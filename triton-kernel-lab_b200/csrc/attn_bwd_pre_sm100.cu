@@ -34,15 +34,16 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, bool bf16) {
   return acc;
 }
 
-// Each group of D/8 threads owns one row; thread g of the group reads the
-// 16-byte chunk g of O and dO (128-bit loads) and clears the matching 32
-// bytes of the dQ accumulator.
-template <int D>
+// Each group of G = DP/8 threads owns one row of d8 = head_dim/8 16-byte
+// chunks (d8 <= G; DP is 64 or 128, the padded width); thread g of the group
+// reads chunk g of O and dO (128-bit loads) and clears the matching 32 bytes
+// of the dQ accumulator, threads g >= d8 idle.
+template <int DP>
 __global__ void __launch_bounds__(kPreThreads)
     attn_bwd_pre_kernel(const uint4* __restrict__ o, const uint4* __restrict__ d_o,
-                        float* __restrict__ delta, float4* __restrict__ dq_accum, long long rows,
+                        float* __restrict__ delta, float4* __restrict__ dq_accum, long long rows, int d8,
                         int bf16) {
-  constexpr int kGroup = D / 8;
+  constexpr int kGroup = DP / 8;
   const long long tid = static_cast<long long>(blockIdx.x) * kPreThreads + threadIdx.x;
   const long long stride = static_cast<long long>(gridDim.x) * kPreThreads;
   const int g = threadIdx.x % kGroup;
@@ -54,14 +55,14 @@ __global__ void __launch_bounds__(kPreThreads)
     const bool live = idx < total;
     const long long row = idx / kGroup;
     float part = 0.0f;
-    if (live) {
-      const uint4 a = o[row * kGroup + g];
-      const uint4 b = d_o[row * kGroup + g];
+    if (live && g < d8) {
+      const uint4 a = o[row * d8 + g];
+      const uint4 b = d_o[row * d8 + g];
       part = dot8(a, b, bf16 != 0);
       if (dq_accum != nullptr) {
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-        dq_accum[row * (D / 4) + 2 * g] = z;
-        dq_accum[row * (D / 4) + 2 * g + 1] = z;
+        dq_accum[row * (2 * d8) + 2 * g] = z;
+        dq_accum[row * (2 * d8) + 2 * g + 1] = z;
       }
     }
 #pragma unroll
@@ -122,17 +123,18 @@ int grid_for(long long work, int threads) {
 
 int launch_attn_bwd_pre(const BwdPreArgs& a) {
   const long long rows = a.BH * a.S;
-  const int grid = grid_for(rows * (a.D / 8), kPreThreads);
-  if (a.D == 64) {
+  if (a.D < 8 || a.D > 128 || a.D % 8 != 0) return kErrUnsupported;
+  const int d8 = static_cast<int>(a.D / 8);
+  if (a.D <= 64) {
+    const int grid = grid_for(rows * 8, kPreThreads);
     attn_bwd_pre_kernel<64><<<grid, kPreThreads, 0, a.stream>>>(
         static_cast<const uint4*>(a.o), static_cast<const uint4*>(a.d_o), a.delta,
-        reinterpret_cast<float4*>(a.dq_accum), rows, a.bf16 ? 1 : 0);
-  } else if (a.D == 128) {
+        reinterpret_cast<float4*>(a.dq_accum), rows, d8, a.bf16 ? 1 : 0);
+  } else {
+    const int grid = grid_for(rows * 16, kPreThreads);
     attn_bwd_pre_kernel<128><<<grid, kPreThreads, 0, a.stream>>>(
         static_cast<const uint4*>(a.o), static_cast<const uint4*>(a.d_o), a.delta,
-        reinterpret_cast<float4*>(a.dq_accum), rows, a.bf16 ? 1 : 0);
-  } else {
-    return kErrUnsupported;
+        reinterpret_cast<float4*>(a.dq_accum), rows, d8, a.bf16 ? 1 : 0);
   }
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }

@@ -139,14 +139,17 @@ __device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const floa
   }
 }
 
-template <int D, bool kBf16>
+// kWithDq false compiles the dQ path out (no dQ product, drain or
+// reduction; tm_dq unused): the dK/dV half of the deterministic backward,
+// whose dQ comes from attn_bwd_dq_kernel.
+template <int D, bool kBf16, bool kWithDq>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
                     const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ lse,
                     const float* __restrict__ delta, int S, int BH, int n_tiles, int causal, float scale,
-                    float scale_log2, unsigned long long timeout_ns, int* status) {
+                    float scale_log2, int d_real, unsigned long long timeout_ns, int* status) {
   using C = BwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -323,7 +326,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       };
       auto issue_dp = [&](int it) -> bool {
         if (!warp_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
-        if (C::kDqAliased && it > 0) {
+        if (kWithDq && C::kDqAliased && it > 0) {
           if (!warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
         }
         tc_fence_after();
@@ -358,17 +361,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         // dQ = dS K  (dS in smem from the dS warps)
         if (!(ok = warp_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
         tc_fence_after();
-        if (!C::kDqAliased && it > 0) {
-          if (!(ok = warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
-        }
-        if (leader) {
+        if constexpr (kWithDq) {
+          if (!C::kDqAliased && it > 0) {
+            if (!(ok = warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
+          }
+          if (leader) {
 #pragma unroll
-          for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_ss_w(tmem + C::kColDQ, ds_mn_lo + mnmajor_koff(kk * 16), k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
-                      kk > 0 ? 1u : 0u);
-          umma_commit(dq_full);
+            for (int kk = 0; kk < kTileRows / 16; ++kk)
+              umma_ss_w(tmem + C::kColDQ, ds_mn_lo + mnmajor_koff(kk * 16), k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
+                        kk > 0 ? 1u : 0u);
+            umma_commit(dq_full);
+          }
+          __syncwarp();
         }
-        __syncwarp();
         // dK += dS^T Q; the smem dS tile is free after this one.
         if (leader) {
 #pragma unroll
@@ -382,7 +387,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
       }
       if (ok) commit(dkdv_done);
-    } else if (warp == 2) {
+    } else if (warp == 2 && kWithDq) {
       // ---------------- dQ reduce issuer ----------------
       bool ok = true;
       for (int it = 0; ok && it < n_steps; ++it) {
@@ -393,8 +398,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (!(ok = warp_wait(stage_full, cnt & 1, ctl, timeout_ns, status, 18))) break;
           if (lane == 0) {
 #pragma unroll
-            for (int bx = 0; bx < 2; ++bx)
-              tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
+            for (int bx = 0; bx < 2; ++bx) {
+              // A head_dim below the kernel's width leaves whole boxes past
+              // the tensor's last column: nothing to add there.
+              if (pass * 64 + bx * 32 < d_real)
+                tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
+            }
             tma_store_commit();
             tma_store_wait_read_all();
             mbar_arrive(stage_free);
@@ -411,7 +420,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = q4 * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
     bool ok = true;
-    for (int it = 0; ok && it < n_steps; ++it) {
+    for (int it = 0; kWithDq && ok && it < n_steps; ++it) {
       if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 16))) break;
       tc_fence_after();
       uint32_t v[D / 32][32];
@@ -568,11 +577,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
 }
 
-template <int D, bool kBf16>
+template <int D, bool kBf16, bool kWithDq>
 int launch_bwd_t(const BwdArgs& a) {
   using C = BwdCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "backward shared memory exceeds the sm_100 limit");
-  auto kern = attn_bwd_kernel<D, kBf16>;
+  auto kern = attn_bwd_kernel<D, kBf16, kWithDq>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -590,17 +599,25 @@ int launch_bwd_t(const BwdArgs& a) {
   const int n_tiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
   const long long grid = static_cast<long long>(n_tiles) * a.BH;
   kern<<<static_cast<unsigned>(grid), kBwdThreads, C::kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, *a.tm_dk, *a.tm_dv, *a.tm_dq, a.lse, a.delta,
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, *a.tm_dk, *a.tm_dv, kWithDq ? *a.tm_dq : *a.tm_dk, a.lse, a.delta,
       static_cast<int>(a.S), static_cast<int>(a.BH), n_tiles, a.causal, a.scale, a.scale_log2,
-      a.timeout_ns, a.status);
+      static_cast<int>(a.D), a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace
 
 int launch_attn_bwd(const BwdArgs& a) {
-  if (a.D == 64) return a.bf16 ? launch_bwd_t<64, true>(a) : launch_bwd_t<64, false>(a);
-  if (a.D == 128) return a.bf16 ? launch_bwd_t<128, true>(a) : launch_bwd_t<128, false>(a);
+  // head_dim <= 64 runs the 64-column kernel, 64 < head_dim <= 128 the
+  // 128-column one; the tensor maps carry the true width.
+  if (a.D <= 64) return a.bf16 ? launch_bwd_t<64, true, true>(a) : launch_bwd_t<64, false, true>(a);
+  if (a.D <= 128) return a.bf16 ? launch_bwd_t<128, true, true>(a) : launch_bwd_t<128, false, true>(a);
+  return kErrUnsupported;
+}
+
+int launch_attn_bwd_dkdv(const BwdArgs& a) {
+  if (a.D <= 64) return a.bf16 ? launch_bwd_t<64, true, false>(a) : launch_bwd_t<64, false, false>(a);
+  if (a.D <= 128) return a.bf16 ? launch_bwd_t<128, true, false>(a) : launch_bwd_t<128, false, false>(a);
   return kErrUnsupported;
 }
 

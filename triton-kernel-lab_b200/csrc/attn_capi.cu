@@ -55,7 +55,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int check_shape(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype) {
   if (batch <= 0 || heads <= 0 || seq <= 0) return tk::kErrInvalidArgument;
-  if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
+  // Any head_dim up to 128 whose rows are 16-byte multiples: the kernels for
+  // 64 and 128 run it with the tensor maps declaring the true width (loads
+  // zero-fill the missing columns, stores and reductions clip them).
+  if (head_dim < 8 || head_dim > 128 || head_dim % 8 != 0) return tk::kErrUnsupported;
   if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
   const int64_t bh = batch * heads;
   if (bh > INT_MAX || seq > INT_MAX) return tk::kErrTooLarge;
@@ -192,6 +195,72 @@ int tk_attn_bwd(const void* q, const void* k, const void* v, const void* d_o, co
                                  head_dim, dtype, causal, scale, stream))
     return rc;
   return tk_attn_dq_convert(dq_accum, dq, batch * heads * seq * head_dim, dtype, stream);
+}
+
+int tk_attn_bwd_dkdv(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                     const float* delta, void* dk, void* dv, int64_t batch, int64_t heads, int64_t seq,
+                     int64_t head_dim, int dtype, int causal, float scale, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || d_o == nullptr || lse == nullptr ||
+      delta == nullptr || dk == nullptr || dv == nullptr)
+    return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(d_o) || !aligned16(dk) || !aligned16(dv))
+    return tk::kErrMisaligned;
+  if ((reinterpret_cast<uintptr_t>(lse) & 3u) || (reinterpret_cast<uintptr_t>(delta) & 3u))
+    return tk::kErrMisaligned;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  const int64_t bh = batch * heads;
+  CUtensorMap mq, mk, mv, mdo, mdk, mdv;
+  if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdo, d_o, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdk, dk, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdv, dv, bh, seq, head_dim, dtype)) return rc;
+  tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, nullptr, lse, delta,
+                bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
+                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
+  return tk::launch_attn_bwd_dkdv(a);
+}
+
+int tk_attn_bwd_dq(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
+                   const float* delta, void* dq, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                   int dtype, int causal, float scale, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || d_o == nullptr || lse == nullptr ||
+      delta == nullptr || dq == nullptr)
+    return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(d_o) || !aligned16(dq))
+    return tk::kErrMisaligned;
+  if ((reinterpret_cast<uintptr_t>(lse) & 3u) || (reinterpret_cast<uintptr_t>(delta) & 3u))
+    return tk::kErrMisaligned;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  const int64_t bh = batch * heads;
+  CUtensorMap mq, mk, mv, mdo, mdq;
+  if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdo, d_o, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mdq, dq, bh, seq, head_dim, dtype)) return rc;
+  tk::BwdDqArgs a{&mq, &mk, &mv, &mdo, &mdq, lse, delta, bh, seq, head_dim, dtype == TK_DTYPE_BF16,
+                  causal ? 1 : 0, scale, scale * kLog2e, g_timeout_ns, status,
+                  static_cast<cudaStream_t>(stream)};
+  return tk::launch_attn_bwd_dq(a);
+}
+
+int tk_attn_bwd_deterministic(const void* q, const void* k, const void* v, const void* o, const void* d_o,
+                              const float* lse, float* delta, void* dq, void* dk, void* dv, int64_t batch,
+                              int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                              void* stream) {
+  if (int rc = tk_attn_bwd_pre(o, d_o, delta, nullptr, batch, heads, seq, head_dim, dtype, stream)) return rc;
+  if (int rc = tk_attn_bwd_dkdv(q, k, v, d_o, lse, delta, dk, dv, batch, heads, seq, head_dim, dtype, causal,
+                                scale, stream))
+    return rc;
+  return tk_attn_bwd_dq(q, k, v, d_o, lse, delta, dq, batch, heads, seq, head_dim, dtype, causal, scale, stream);
 }
 
 size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim) {

@@ -463,8 +463,10 @@ int launch_fwd_t(const FwdArgs& a) {
 }  // namespace
 
 int launch_attn_fwd(const FwdArgs& a) {
-  if (a.D == 64) return a.bf16 ? launch_fwd_t<64, true>(a) : launch_fwd_t<64, false>(a);
-  if (a.D == 128) return a.bf16 ? launch_fwd_t<128, true>(a) : launch_fwd_t<128, false>(a);
+  // head_dim <= 64 runs the 64-column kernel, 64 < head_dim <= 128 the
+  // 128-column one; the tensor maps carry the true width.
+  if (a.D <= 64) return a.bf16 ? launch_fwd_t<64, true>(a) : launch_fwd_t<64, false>(a);
+  if (a.D <= 128) return a.bf16 ? launch_fwd_t<128, true>(a) : launch_fwd_t<128, false>(a);
   return kErrUnsupported;
 }
 

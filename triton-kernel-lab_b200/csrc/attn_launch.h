@@ -53,6 +53,25 @@ struct BwdArgs {
   cudaStream_t stream;
 };
 
+// Deterministic dQ kernel (query-stationary, no atomics).
+struct BwdDqArgs {
+  const CUtensorMap* tm_q;
+  const CUtensorMap* tm_k;
+  const CUtensorMap* tm_v;
+  const CUtensorMap* tm_do;
+  const CUtensorMap* tm_dq;  // 16-bit dQ output
+  const float* lse;
+  const float* delta;
+  int64_t BH, S, D;
+  bool bf16;
+  int causal;
+  float scale;
+  float scale_log2;
+  unsigned long long timeout_ns;
+  int* status;
+  cudaStream_t stream;
+};
+
 struct DqConvertArgs {
   const float* dq_accum;
   void* dq;
@@ -64,6 +83,10 @@ struct DqConvertArgs {
 int launch_attn_fwd(const FwdArgs& a);
 int launch_attn_bwd_pre(const BwdPreArgs& a);
 int launch_attn_bwd(const BwdArgs& a);
+// The fused backward with its dQ path compiled out (dK and dV only; a.tm_dq
+// is not read).
+int launch_attn_bwd_dkdv(const BwdArgs& a);
+int launch_attn_bwd_dq(const BwdDqArgs& a);
 int launch_attn_dq_convert(const DqConvertArgs& a);
 int launch_wait_timeout_selftest(unsigned long long timeout_ns, int* status, cudaStream_t stream);
 int launch_umma_diag(const CUtensorMap* tm_a, const CUtensorMap* tm_b, const uint32_t* a_words, float* c,

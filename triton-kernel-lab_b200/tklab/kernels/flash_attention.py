@@ -13,7 +13,9 @@ raises.
 
 Contract differences from the reference, all widenings:
 * dtypes float16 and bfloat16 (reference: float16 only, ``:281-282``);
-* head_dim 64 or 128 (reference: 64 only, ``:283-284``).
+* head_dim any multiple of 8 from 8 to 128 (reference: 64 only,
+  ``:283-284``); widths below 64 / 128 run the 64- / 128-column kernels with
+  the tensor maps declaring the true width.
 """
 
 from __future__ import annotations
@@ -46,25 +48,32 @@ _BATCH = 1
 _HEADS = 16
 _HEAD_DIM = 64
 
-SUPPORTED_HEAD_DIMS = (64, 128)
+# Head dims the kernels accept: multiples of 8 (16-byte rows for TMA) up to
+# 128.  64 and 128 are the kernels' native widths.
+MAX_HEAD_DIM = 128
+SUPPORTED_HEAD_DIMS = tuple(range(8, MAX_HEAD_DIM + 1, 8))
 _NATIVE_DTYPE = {torch.float16: _native.TK_DTYPE_F16, torch.bfloat16: _native.TK_DTYPE_BF16}
 
-# Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile,
-# forward CTA = 6 warps, K/V ring depth 4 (head_dim 64) or 2 (head_dim 128).
+# Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile
+# (a forward CTA runs two query tiles), forward CTA = 12 warps, backward CTA
+# = 16 warps, K/V ring depth 4 (head_dim <= 64) or 2 (head_dim <= 128).
 _BLOCK_M = 128
 _BLOCK_N = 128
-_FWD_WARPS = 6
-_BWD_WARPS = 10
+_FWD_WARPS = 12
+_BWD_WARPS = 16
 
 
 def _fwd_stages(head_dim: int) -> int:
-    return 4 if head_dim == 64 else 2
+    return 4 if head_dim <= 64 else 2
 
 
 # Set TKLAB_CHECK_DEVICE_STATUS=1 to synchronise after every launch and raise
 # on a device-side error (bounded wait that ran out).  Off by default so
 # launches stay asynchronous like the reference's Triton launches.
 _CHECK_STATUS = os.environ.get("TKLAB_CHECK_DEVICE_STATUS", "0") == "1"
+# TKLAB_DETERMINISTIC_BWD=1 makes the backward use the deterministic path
+# (no floating-point atomics) even when torch's deterministic mode is off.
+_DETERMINISTIC_ENV = os.environ.get("TKLAB_DETERMINISTIC_BWD", "0") == "1"
 
 
 def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -84,7 +93,7 @@ def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
     if q.dtype not in _NATIVE_DTYPE:
         raise ValueError("attention currently supports float16 and bfloat16 inputs only")
     if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
-        raise ValueError(f"attention currently requires head_dim in {SUPPORTED_HEAD_DIMS}")
+        raise ValueError(f"attention currently requires head_dim to be a multiple of 8 from 8 to {MAX_HEAD_DIM}")
     for name, tensor in (("Q", q), ("K", k), ("V", v)):
         if not tensor.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
@@ -192,12 +201,19 @@ def _launch_backward(
     do: torch.Tensor,
     *,
     causal: bool,
+    deterministic: bool | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Run the recompute backward and return ``(dQ, dK, dV)`` (reference ``:536-607``).
 
-    Two library calls: ``tk_attn_bwd_pre`` (delta = rowsum(dO * O) and a
-    cleared fp32 dQ accumulator) and ``tk_attn_bwd`` (the fused tcgen05
-    kernel for dK, dV and dQ, then the dQ conversion).
+    Default: two library calls, ``tk_attn_bwd_pre`` (delta = rowsum(dO * O)
+    and a cleared fp32 dQ accumulator) and ``tk_attn_bwd`` (the fused tcgen05
+    kernel for dK, dV and dQ, dQ added across key tiles by TMA reduce-add,
+    then the dQ conversion).  ``deterministic`` (default: on when
+    ``torch.are_deterministic_algorithms_enabled()`` or the environment sets
+    ``TKLAB_DETERMINISTIC_BWD=1``) runs ``tk_attn_bwd_deterministic``
+    instead: dK/dV from the fused kernel without its dQ path and dQ from a
+    query-stationary kernel that sums the key tiles in one fixed order, so
+    repeated calls return bitwise identical gradients.
     """
     if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
         raise ValueError("attention upstream gradient metadata must match Q")
@@ -210,13 +226,25 @@ def _launch_backward(
         or not softmax_lse.is_contiguous()
     ):
         raise ValueError("attention log-sum-exp buffer must be contiguous float32 BxHxN")
+    if deterministic is None:
+        deterministic = torch.are_deterministic_algorithms_enabled() or _DETERMINISTIC_ENV
     delta = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
-    dq_accum = torch.empty((batch, heads, n_ctx, head_dim), dtype=torch.float32, device=q.device)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     lib = _native.load()
     dtype = _NATIVE_DTYPE[q.dtype]
+    if deterministic:
+        with torch.cuda.device(q.device):
+            status = lib.tk_attn_bwd_deterministic(
+                q.data_ptr(), k.data_ptr(), v.data_ptr(), output.data_ptr(), do.data_ptr(),
+                softmax_lse.data_ptr(), delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                batch, heads, n_ctx, head_dim, dtype, int(bool(causal)), 1.0 / math.sqrt(head_dim), _stream(q),
+            )
+            _native.check(status, "tk_attn_bwd_deterministic")
+        _after_launch(q.device)
+        return dq, dk, dv
+    dq_accum = torch.empty((batch, heads, n_ctx, head_dim), dtype=torch.float32, device=q.device)
     with torch.cuda.device(q.device):
         stream = _stream(q)
         status = lib.tk_attn_bwd_pre(
