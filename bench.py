@@ -77,11 +77,14 @@ def bwd_flops(b: int, h: int, s: int, d: int, causal: bool) -> int:
 
 
 class ClockSampler:
-    """Streams ``nvidia-smi -lms 100`` clock / throttle-reason samples while active."""
+    """Streams ``nvidia-smi -lms 20`` clock / throttle-reason samples, each
+    stamped with the host monotonic clock, so that the samples falling inside
+    a timed window can be picked out afterwards."""
 
-    def __init__(self, index: int) -> None:
+    def __init__(self, index: int, interval_ms: int = 20) -> None:
         self.index = index
-        self.samples: list[tuple[float, float, int]] = []
+        self.interval_ms = interval_ms
+        self.samples: list[tuple[float, float, float, int]] = []
         self._proc: subprocess.Popen | None = None
         self._thread = threading.Thread(target=self._read, daemon=True)
 
@@ -90,7 +93,7 @@ class ClockSampler:
         for line in self._proc.stdout:
             try:
                 sm, sm_max, reasons = (x.strip() for x in line.split(","))
-                self.samples.append((float(sm), float(sm_max), int(reasons, 16)))
+                self.samples.append((time.monotonic(), float(sm), float(sm_max), int(reasons, 16)))
             except ValueError:
                 continue
 
@@ -99,13 +102,19 @@ class ClockSampler:
         try:
             self._proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={query}", "--format=csv,noheader,nounits",
-                 "-lms", "100"],
+                 "-lms", str(self.interval_ms)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
             )
             self._thread.start()
         except OSError:
             self._proc = None
         return self
+
+    def wait_first(self, timeout_s: float = 5.0) -> None:
+        """Block until the first sample has arrived (nvidia-smi takes a moment to start)."""
+        deadline = time.monotonic() + timeout_s
+        while self._proc is not None and not self.samples and time.monotonic() < deadline:
+            time.sleep(0.01)
 
     def __exit__(self, *exc: object) -> None:
         if self._proc is not None:
@@ -116,18 +125,28 @@ class ClockSampler:
                 self._proc.kill()
             self._thread.join(timeout=5)
 
-    def summary(self) -> dict:
-        if not self.samples:
+    def summary(self, t0: float | None = None, t1: float | None = None) -> dict:
+        """Summary of the samples taken in [t0, t1] (all samples when no window is given).
+        A window shorter than the sampling interval may hold none: then the
+        first samples after t0, within two intervals of t1, are used."""
+        picked = list(self.samples)
+        if t0 is not None and t1 is not None:
+            inside = [x for x in self.samples if t0 <= x[0] <= t1]
+            if not inside:
+                slack = 2 * self.interval_ms / 1000.0
+                inside = [x for x in self.samples if t0 <= x[0] <= t1 + slack][:2]
+            picked = inside
+        if not picked:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         mask = 0
-        for _, _, r in self.samples:
+        for _, _, _, r in picked:
             mask |= r
         reasons = [name for bit, name in THROTTLE_REASONS.items() if mask & bit and bit != 0x1]
         return {
-            "sm_mhz": statistics.median(s for s, _, _ in self.samples),
-            "sm_max_mhz": max(m for _, m, _ in self.samples),
+            "sm_mhz": statistics.median(s for _, s, _, _ in picked),
+            "sm_max_mhz": max(m for _, _, m, _ in picked),
             "reasons": reasons,
-            "samples": len(self.samples),
+            "samples": len(picked),
         }
 
 
@@ -202,27 +221,36 @@ def run_ours(args: argparse.Namespace) -> None:
         _native.check(lib.tk_attn_dq_convert(dq_accum.data_ptr(), dq.data_ptr(), numel, nd, sp), "dq_convert")
         mark(4)
 
-    for _ in range(args.warmup):
-        flush.zero_()
-        step(None)
-    torch.cuda.synchronize(device)
-    status = _native.device_status(sp)
-    if status:
-        _native.check(status, "warm-up device status")
-
-    events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize(device)
+    # The clock sampler runs from before the warm-up so that its samples
+    # cover the whole timed region, however short.
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if sampler:
         sampler.__enter__()
-    for i in range(args.steps):
-        flush.zero_()  # write > L2 (126 MB) between timed steps, outside the step's events
-        step(events[i])
-    torch.cuda.synchronize(device)
-    if sampler:
-        sampler.__exit__()
+        sampler.wait_first()
+    try:
+        for _ in range(args.warmup):
+            flush.zero_()
+            step(None)
+        torch.cuda.synchronize(device)
+        status = _native.device_status(sp)
+        if status:
+            _native.check(status, "warm-up device status")
+
+        events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+        t_start = time.monotonic()
+        for i in range(args.steps):
+            flush.zero_()  # write > L2 (126 MB) between timed steps, outside the step's events
+            step(events[i])
+        torch.cuda.synchronize(device)
+        t_end = time.monotonic()
+        if sampler:
+            time.sleep(2 * sampler.interval_ms / 1000.0)
+    finally:
+        if sampler:
+            sampler.__exit__()
     if world > 1:
         torch.distributed.barrier()
     status = _native.device_status(sp)
@@ -263,7 +291,7 @@ def run_ours(args: argparse.Namespace) -> None:
         dom = max(kernels, key=lambda n: kernels[n][0])
         dom_ms, dom_flops = kernels[dom]
         achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-        clocks = sampler.summary() if sampler else None
+        clocks = sampler.summary(t_start, t_end) if sampler else None
         line = {
             "metric": "attention fwd+bwd TFLOP/s (causal bf16 B=8 H=32 S=4096 D=128), aggregate over GPUs",
             "value": round(value, 2),
