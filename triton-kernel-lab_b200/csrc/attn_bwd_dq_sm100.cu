@@ -13,18 +13,26 @@
 // scale at the end (:532).
 //
 // 12 warps in three warpgroups (setmaxnreg 56 / 224 / 224):
-//   WG0  warp 0   TMA producer (Q and dO once, K and V through rings)
+//   WG0  warp 0   TMA producer of Q and dO (once) and the K ring
 //        warp 1   TMEM allocator and tcgen05.mma issuer (converged warp, one
 //                 elected lane issues)
+//        warp 2   TMA producer of the V ring
 //   WG1, WG2  keys 0..63 (WG1) and 64..127 (WG2) of every key tile; thread
 //             t owns query row t (TMEM lane t).  Per key tile: load its
 //             halves of S and dP, release them, form P and dS in registers,
 //             write dS packed to 16 bits into TMEM (the A operand of
 //             dQ += dS.K).  Epilogue: each stores one column half of dQ.
-// Tensor memory: S [0,128), dP [128,256), dQ [256,256+D), dS [256+D,+64).
+// Tensor memory: S [0,128), dP [128,256), dQ [256,256+D), dS in two 64-column
+// buffers from 256+D (tile j uses buffer j&1).
 // MMA order per key tile j: S(j+1) and dP(j+1) as soon as the compute warps
 // have read S(j) and dP(j), then dQ += dS(j).K(j), so the products of the next
-// tile run while the compute warps work on the current one.
+// tile run while the compute warps work on the current one; S/dP go first
+// because the compute warps wait for them next.  A tcgen05.commit tracks every
+// earlier MMA of the issuing thread, and dQ(j-1) is issued before S(j+1), so
+// the completion of S(j+1) (sdp_full) also means dQ(j-1) has read dS buffer
+// (j+1)&1: the compute warps need no separate "dS free" wait.  (Issuing dQ
+// from a second warp was measured slower: its MMAs then interleave with
+// S(j+1)/dP(j+1) and delay the products the compute warps wait for.)
 #include "attn_launch.h"
 #include "sm100_primitives.cuh"
 
@@ -42,16 +50,19 @@ struct DqCfg {
   static constexpr int kKOff = kDOOff + kTileBytes;
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
-  // qdo_full, k_full[KS], k_empty[KS], v_full[VS], v_empty[VS], sdp_full,
-  // sdp_free, ds_ready, ds_free, dq_done
-  static constexpr int kNumBars = 1 + 2 * kKStages + 2 * kVStages + 5;
+  // qdo_full, kv_full[KS], k_empty[KS], v_empty[VS], sdp_full, sdp_free,
+  // ds_ready, dq_done.  K_j and V_j land on one barrier, kv_full[j % KS]
+  // (two producer arrivals plus both tiles' bytes), so the MMA warp polls
+  // once per tile for its operands.
+  static constexpr int kNumBars = 1 + 2 * kKStages + kVStages + 4;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColS = 0;
   static constexpr uint32_t kColDP = 128;
   static constexpr uint32_t kColDQ = 256;
-  static constexpr uint32_t kColDS = 256 + D;
+  static constexpr uint32_t kColDS = 256 + D;  // two buffers of 64 columns
+  static_assert(kColDS + 128 <= kTmemCols, "tensor memory overflow");
 };
 
 constexpr int kDqThreads = 384;
@@ -97,31 +108,25 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   uint8_t* sV = smem + C::kVOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* qdo_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* k_empty = k_full + C::kKStages;
-  uint64_t* v_full = k_empty + C::kKStages;
-  uint64_t* v_empty = v_full + C::kVStages;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* k_empty = kv_full + C::kKStages;
+  uint64_t* v_empty = k_empty + C::kKStages;
   uint64_t* sdp_full = v_empty + C::kVStages;
   uint64_t* sdp_free = sdp_full + 1;
   uint64_t* ds_ready = sdp_free + 1;
-  uint64_t* ds_free = ds_ready + 1;
-  uint64_t* dq_done = ds_free + 1;
+  uint64_t* dq_done = ds_ready + 1;
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
     mbar_init(qdo_full, 1);
     for (int i = 0; i < C::kKStages; ++i) {
-      mbar_init(&k_full[i], 1);
+      mbar_init(&kv_full[i], 2);  // the K and the V producer
       mbar_init(&k_empty[i], 1);
     }
-    for (int i = 0; i < C::kVStages; ++i) {
-      mbar_init(&v_full[i], 1);
-      mbar_init(&v_empty[i], 1);
-    }
+    for (int i = 0; i < C::kVStages; ++i) mbar_init(&v_empty[i], 1);
     mbar_init(sdp_full, 1);
     mbar_init(sdp_free, 8);  // every warp of both compute warpgroups
     mbar_init(ds_ready, 8);
-    mbar_init(ds_free, 1);
     mbar_init(dq_done, 1);
     ctl->abort = 0;
     fence_mbarrier_init();
@@ -150,17 +155,27 @@ __global__ void __launch_bounds__(kDqThreads, 1)
         tma_load_3d(sDO + b * kBlockBytes, &tm_do, qdo_full, b * 64, m0, bh);
       }
       for (int j = 0; j < n_kv; ++j) {
-        const int ks = j % C::kKStages, vs = j % C::kVStages;
+        const int ks = j % C::kKStages;
         if (!mbar_wait(&k_empty[ks], ((j / C::kKStages) & 1) ^ 1, ctl, timeout_ns, status, 1)) break;
-        mbar_arrive_expect_tx(&k_full[ks], C::kTileBytes);
+        mbar_arrive_expect_tx(&kv_full[ks], C::kTileBytes);
 #pragma unroll
         for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sK + ks * C::kTileBytes + b * kBlockBytes, &tm_k, &k_full[ks], b * 64, j * kTileRows, bh);
+          tma_load_3d(sK + ks * C::kTileBytes + b * kBlockBytes, &tm_k, &kv_full[ks], b * 64, j * kTileRows, bh);
+      }
+    } else if (warp == 2 && lane == 0) {
+      // ---------------- V producer: its own thread, so a V load never waits
+      // behind a K slot (K_j is held until dQ(j), V_j only until dP(j)).
+      // kv_full[j % KS] cannot receive tile j+KS's arrivals before tile j's
+      // phase completes: K_{j+KS} waits for dQ(j) and V_{j+KS} for
+      // dP(j+KS-VS), both issued only after that phase. ----------------
+      for (int j = 0; j < n_kv; ++j) {
+        const int vs = j % C::kVStages;
         if (!mbar_wait(&v_empty[vs], ((j / C::kVStages) & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
-        mbar_arrive_expect_tx(&v_full[vs], C::kTileBytes);
+        uint64_t* full = &kv_full[j % C::kKStages];
+        mbar_arrive_expect_tx(full, C::kTileBytes);
 #pragma unroll
         for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sV + vs * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[vs], b * 64, j * kTileRows, bh);
+          tma_load_3d(sV + vs * C::kTileBytes + b * kBlockBytes, &tm_v, full, b * 64, j * kTileRows, bh);
       }
     } else if (warp == 1) {
       // ---------------- MMA issuer ----------------
@@ -174,53 +189,62 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       const uint32_t k_mn_lo0 = sdesc_lo_mnmajor(smem_u32(sK), kTileRows);
       const uint32_t v_lo0 = sdesc_lo_kmajor(smem_u32(sV));
       constexpr uint32_t kTileLo = C::kTileBytes >> 4;
-      // S(j) = Q K_j^T and dP(j) = dO V_j^T into their TMEM columns.
-      auto issue_sdp = [&](int j) -> bool {
-        const int ks = j % C::kKStages, vs = j % C::kVStages;
-        if (!warp_wait(&k_full[ks], (j / C::kKStages) & 1, ctl, timeout_ns, status, 3)) return false;
-        if (!warp_wait(&v_full[vs], (j / C::kVStages) & 1, ctl, timeout_ns, status, 4)) return false;
-        tc_fence_after();
-        const uint32_t k_lo = k_lo0 + ks * kTileLo;
-        const uint32_t v_lo = v_lo0 + vs * kTileLo;
-        if (leader) {
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss_w(tmem + C::kColS, q_lo + kmajor_koff(kTileRows, kk * 16), k_lo + kmajor_koff(kTileRows, kk * 16),
-                      idesc_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            umma_ss_w(tmem + C::kColDP, do_lo + kmajor_koff(kTileRows, kk * 16),
-                      v_lo + kmajor_koff(kTileRows, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
-          umma_commit(sdp_full);
-          umma_commit(&v_empty[vs]);  // V_j is only read by dP(j)
-        }
-        __syncwarp();
-        return true;
-      };
+      // tcgen05.mma issue blocks at about the tensor core's execution rate
+      // and only a few MMAs queue ahead of it, so every barrier poll of this
+      // warp between two MMA batches risks idling the tensor core.  The loop
+      // therefore has at most two polls after the S/dP batch (the next
+      // tile's operands and ds_ready) and one after the dQ batch (sdp_free),
+      // each normally satisfied already and covered by the queued MMAs.
+      // One copy of each step and rolled MMA loops keep the code compact:
+      // this warp sleeps while the compute warps stream long unrolled bodies
+      // through the instruction cache.
+      //
+      // Step t: S(t) and dP(t) once the compute warps have read S(t-1) and
+      // dP(t-1), then dQ += dS(t-1) K_{t-1}.
       bool ok = warp_wait(qdo_full, 0, ctl, timeout_ns, status, 5);
-      if (ok && n_kv > 0) ok = issue_sdp(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int ks = j % C::kKStages;
-        // The next tile's products overwrite S and dP: wait until the
-        // compute warps have read this tile's.
-        if (j + 1 < n_kv) {
-          if (!(ok = warp_wait(sdp_free, j & 1, ctl, timeout_ns, status, 6))) break;
-          if (!(ok = issue_sdp(j + 1))) break;
+      if (ok && n_kv > 0) ok = warp_wait(&kv_full[0], 0, ctl, timeout_ns, status, 3);
+      for (int t = 0; ok && t <= n_kv; ++t) {
+        if (t < n_kv) {
+          const int ks = t % C::kKStages, vs = t % C::kVStages;
+          if (t > 0 && !(ok = warp_wait(sdp_free, (t - 1) & 1, ctl, timeout_ns, status, 6))) break;
+          tc_fence_after();
+          if (leader) {
+            const uint32_t k_lo = k_lo0 + ks * kTileLo;
+            const uint32_t v_lo = v_lo0 + vs * kTileLo;
+#pragma unroll 1
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = kmajor_koff(kTileRows, kk * 16);
+              const uint32_t acc = kk > 0 ? 1u : 0u;
+              umma_ss_w(tmem + C::kColS, q_lo + off, k_lo + off, idesc_s, acc);
+              umma_ss_w(tmem + C::kColDP, do_lo + off, v_lo + off, idesc_s, acc);
+            }
+            umma_commit(sdp_full);
+            umma_commit(&v_empty[vs]);  // V_t is only read by dP(t)
+          }
+          __syncwarp();
+          const int tn = t + 1;
+          if (tn < n_kv &&
+              !(ok = warp_wait(&kv_full[tn % C::kKStages], (tn / C::kKStages) & 1, ctl, timeout_ns, status, 4)))
+            break;
         }
-        // dQ += dS(j) K_j with dS(j) packed in TMEM.
-        if (!(ok = warp_wait(ds_ready, j & 1, ctl, timeout_ns, status, 7))) break;
-        tc_fence_after();
-        const uint32_t k_mn_lo = k_mn_lo0 + ks * kTileLo;
-        if (leader) {
-#pragma unroll
-          for (int kk = 0; kk < kTileRows / 16; ++kk)
-            umma_ts_w(tmem + C::kColDQ, tmem + C::kColDS + kk * 8, k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
-                      (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(ds_free);
-          umma_commit(&k_empty[ks]);  // K_j was read by S(j) and dQ(j)
-          if (j + 1 == n_kv) umma_commit(dq_done);
+        if (t > 0) {
+          // dQ += dS(j) K_j with dS(j) packed in TMEM buffer j&1.
+          const int j = t - 1;
+          const int ks = j % C::kKStages;
+          if (!(ok = warp_wait(ds_ready, j & 1, ctl, timeout_ns, status, 7))) break;
+          tc_fence_after();
+          if (leader) {
+            const uint32_t k_mn_lo = k_mn_lo0 + ks * kTileLo;
+            const uint32_t ds_col = tmem + C::kColDS + 64u * (j & 1);
+#pragma unroll 1
+            for (int kk = 0; kk < kTileRows / 16; ++kk)
+              umma_ts_w(tmem + C::kColDQ, ds_col + kk * 8, k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
+                        (j > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&k_empty[ks]);  // K_j was read by S(j) and dQ(j)
+            if (t == n_kv) umma_commit(dq_done);
+          }
+          __syncwarp();
         }
-        __syncwarp();
       }
     }
   } else {
@@ -277,11 +301,9 @@ __global__ void __launch_bounds__(kDqThreads, 1)
           pk[b][c >> 1] = pack2<kBf16>(d0, d1);
         }
       }
-      // The dS buffer is free once dQ(j-1) has read it.
-      if (j > 0 && !(ok = warp_wait(ds_free, (j - 1) & 1, ctl, timeout_ns, status, 9))) break;
-      tc_fence_after();
-      tmem_st16(ds_cols, pk[0]);
-      tmem_st16(ds_cols + 16, pk[1]);
+      // dS buffer j&1 was last read by dQ(j-2), complete since sdp_full(j).
+      tmem_st16(ds_cols + 64u * (j & 1), pk[0]);
+      tmem_st16(ds_cols + 64u * (j & 1) + 16, pk[1]);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
