@@ -75,9 +75,14 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaCon
 }
 
 // Of every 8 column pairs of an unmasked tile, this many take their exp2 on
-// the FMA pipe (exp2_fma) and the rest on the MUFU, which alone would bound a
-// tile at 1024 cycles (16384 exponentials at 16 per clock).
-constexpr int kEmuPairsPer8 = 0;
+// the FMA pipe (exp2_fma_pair, packed fp32x2 arithmetic) and the rest on the
+// MUFU, which alone would bound a tile at 1024 cycles (16384 exponentials at
+// 16 per clock per SM) while the rest of the softmax needs about three issue
+// slots per element.
+#ifndef TK_FWD_EMU_PAIRS_PER8
+#define TK_FWD_EMU_PAIRS_PER8 3
+#endif
+constexpr int kEmuPairsPer8 = TK_FWD_EMU_PAIRS_PER8;
 
 template <bool kMasked>
 __device__ __forceinline__ void max_chunk(uint32_t (&s)[32], int col0, int lim, float (&mx)[8]) {
@@ -131,30 +136,35 @@ __device__ __forceinline__ void softmax_tile(uint32_t s_addr, int lim, float sca
   const float m_use = need ? m_new : m_run;
   alpha = (m_run == -INFINITY) ? 0.0f : ex2(m_run - m_use);
   const float ms = (m_use == -INFINITY) ? 0.0f : m_use;
-  float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  // x = s * scale_log2 - max and the row sum run on packed pairs.
+  const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+  const uint64_t negm2 = f2_pack(-ms, -ms);
+  uint64_t sum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
     uint32_t pk[16];
 #pragma unroll
     for (int c = 0; c < 32; c += 2) {
-      const float x0 = fmaf(__uint_as_float(s[b][c]), scale_log2, -ms);
-      const float x1 = fmaf(__uint_as_float(s[b][c + 1]), scale_log2, -ms);
+      float x0, x1;
+      f2_unpack(ffma2(f2_pack(__uint_as_float(s[b][c]), __uint_as_float(s[b][c + 1])), scale2, negm2), x0, x1);
       float p0, p1;
       // Masked tiles keep every exponential on the MUFU so that masked
       // entries are exactly zero.
       if (!kMasked && ((c >> 1) & 7) >= 8 - kEmuPairsPer8) {
-        p0 = exp2_fma(x0);
-        p1 = exp2_fma(x1);
+        exp2_fma_pair(x0, x1, p0, p1);
       } else {
         p0 = ex2(x0);
         p1 = ex2(x1);
       }
-      sum[(c >> 1) & 3] += p0 + p1;
+      sum2[(c >> 1) & 1] = fadd2(sum2[(c >> 1) & 1], f2_pack(p0, p1));
       pk[c >> 1] = pack2<kBf16>(p0, p1);
     }
     tmem_st16(s_addr + b * 16, pk);
   }
-  l_run = l_run * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+  float sa0, sa1, sb0, sb1;
+  f2_unpack(sum2[0], sa0, sa1);
+  f2_unpack(sum2[1], sb0, sb1);
+  l_run = l_run * alpha + ((sa0 + sa1) + (sb0 + sb1));
   m_run = m_use;
 }
 
