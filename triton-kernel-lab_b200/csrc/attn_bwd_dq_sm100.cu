@@ -262,6 +262,9 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     const bool row_ok = row_g < S;
     const float lse_r = row_ok ? lse[static_cast<size_t>(bh) * S + row_g] : INFINITY;
     const float delta_r = row_ok ? delta[static_cast<size_t>(bh) * S + row_g] : 0.0f;
+    const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    const uint64_t nlse2 = f2_pack(-lse_r, -lse_r);
+    const uint64_t ndelta2 = f2_pack(-delta_r, -delta_r);
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       if (!(ok = warp_wait(sdp_full, j & 1, ctl, timeout_ns, status, 8))) break;
@@ -290,14 +293,19 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       for (int b = 0; b < 2; ++b) {
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
-          float p0 = ex2(fmaf(__uint_as_float(s[b][c]), scale_log2, -lse_r));
-          float p1 = ex2(fmaf(__uint_as_float(s[b][c + 1]), scale_log2, -lse_r));
+          // Pairs of keys per packed fp32x2 instruction.
+          float x0, x1;
+          f2_unpack(ffma2(f2_pack(__uint_as_float(s[b][c]), __uint_as_float(s[b][c + 1])), scale2, nlse2), x0, x1);
+          float p0 = ex2(x0);
+          float p1 = ex2(x1);
           if (masked) {
             if (b * 32 + c >= lim) p0 = 0.0f;
             if (b * 32 + c + 1 >= lim) p1 = 0.0f;
           }
-          const float d0 = p0 * (__uint_as_float(dp[b][c]) - delta_r);
-          const float d1 = p1 * (__uint_as_float(dp[b][c + 1]) - delta_r);
+          float d0, d1;
+          f2_unpack(fmul2(f2_pack(p0, p1),
+                          fadd2(f2_pack(__uint_as_float(dp[b][c]), __uint_as_float(dp[b][c + 1])), ndelta2)),
+                    d0, d1);
           pk[b][c >> 1] = pack2<kBf16>(d0, d1);
         }
       }

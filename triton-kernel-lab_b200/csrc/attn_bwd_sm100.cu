@@ -115,22 +115,29 @@ __device__ __forceinline__ void stage_row(uint32_t t_row, uint8_t* tile, int r, 
 }
 
 // P^T for 32 queries of one key row: p = exp2(s * scale*log2(e) - LSE2[q]).
-// The 32 LSE values are read with 128-bit broadcast loads (every lane of the
-// warp reads the same address).  kMasked adds the causal diagonal (query q0+e
-// is dropped when it precedes this thread's key, diag_key) and the ragged key
-// tail (key_ok false: the whole row is zero).
+// nlse_s holds the negated LSE values, read with 128-bit broadcast loads
+// (every lane of the warp reads the same address), so each pair's argument
+// is one packed fma.  kMasked adds the causal diagonal (query q0+e is dropped
+// when it precedes this thread's key, diag_key) and the ragged key tail
+// (key_ok false: the whole row is zero).
 template <bool kMasked>
-__device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const float* lse_s, float scale_log2,
+__device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const float* nlse_s, float scale_log2,
                                             int q0, int diag_key, bool key_ok, float (&p)[32]) {
-  const float4* lse4 = reinterpret_cast<const float4*>(lse_s);
+  const float4* nlse4 = reinterpret_cast<const float4*>(nlse_s);
+  const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
   for (int e4 = 0; e4 < 8; ++e4) {
-    const float4 l = lse4[e4];
-    const float lv[4] = {l.x, l.y, l.z, l.w};
+    const float4 l = nlse4[e4];
+    float x[4];
+    const int e0 = e4 * 4;
+    f2_unpack(ffma2(f2_pack(__uint_as_float(sv[e0]), __uint_as_float(sv[e0 + 1])), scale2, f2_pack(l.x, l.y)), x[0],
+              x[1]);
+    f2_unpack(ffma2(f2_pack(__uint_as_float(sv[e0 + 2]), __uint_as_float(sv[e0 + 3])), scale2, f2_pack(l.z, l.w)),
+              x[2], x[3]);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int e = e4 * 4 + j;
-      float pv = ex2(fmaf(__uint_as_float(sv[e]), scale_log2, -lv[j]));
+      const int e = e0 + j;
+      float pv = ex2(x[j]);
       if constexpr (kMasked) {
         if (q0 + e < diag_key || !key_ok) pv = 0.0f;
       }
@@ -270,8 +277,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int b = 0; b < D / 64; ++b) tma_load_3d(sDO + b * kBlockBytes, &tm_do, do_full, b * 64, m0, bh);
         }
-        // LSE / delta for this query step.  Padded queries get LSE = +inf so
-        // their probabilities are exactly zero.
+        // -LSE / delta for this query step (LSE stored negated for the
+        // packed P argument).  Padded queries get -LSE = -inf so their
+        // probabilities are exactly zero.
         const int lb = it & 1;
         if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 3)) break;
 #pragma unroll
@@ -279,7 +287,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const int q = e * 32 + lane;
           const int mg = m0 + q;
           const bool valid = mg < S;
-          sLse[lb * 128 + q] = valid ? lse[row_base + mg] : INFINITY;
+          sLse[lb * 128 + q] = valid ? -lse[row_base + mg] : -INFINITY;
           sDelta[lb * 128 + q] = valid ? delta[row_base + mg] : 0.0f;
         }
         mbar_arrive(&ld_full[lb]);
@@ -471,7 +479,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 12))) break;
       tc_fence_after();
       const bool diag = causal && (i == jn);
-      const float* lse_s = sLse + lb * 128 + h * 64;
+      const float* nlse_s = sLse + lb * 128 + h * 64;
       const float* del_s = sDelta + lb * 128 + h * 64;
       // Phase 1: P^T for this warpgroup's 64 queries -> registers and,
       // packed to 16 bits, back over the first 32 of its S columns (both
@@ -489,9 +497,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           if (masked)
-            probs_chunk<true>(sv[c], lse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
+            probs_chunk<true>(sv[c], nlse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
           else
-            probs_chunk<false>(sv[c], lse_s + c * 32, scale_log2, 0, 0, true, p[c]);
+            probs_chunk<false>(sv[c], nlse_s + c * 32, scale_log2, 0, 0, true, p[c]);
         }
       }
 #pragma unroll
@@ -522,14 +530,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const uint32_t (&dpv)[32] = dpv2[c];
         uint32_t dd[16];
         const float4* del4 = reinterpret_cast<const float4*>(del_s + c * 32);
+        const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
 #pragma unroll
         for (int e4 = 0; e4 < 8; ++e4) {
           const float4 dl = del4[e4];  // one broadcast 128-bit load for 4 queries
           const int e = e4 * 4;
-          dd[e4 * 2] = pack2<kBf16>(p[c][e] * (__uint_as_float(dpv[e]) - dl.x),
-                                    p[c][e + 1] * (__uint_as_float(dpv[e + 1]) - dl.y));
-          dd[e4 * 2 + 1] = pack2<kBf16>(p[c][e + 2] * (__uint_as_float(dpv[e + 2]) - dl.z),
-                                        p[c][e + 3] * (__uint_as_float(dpv[e + 3]) - dl.w));
+          // dS = P (dP - delta), two queries per packed instruction.
+          float d0, d1, d2, d3;
+          f2_unpack(fmul2(f2_pack(p[c][e], p[c][e + 1]),
+                          ffma2(f2_pack(dl.x, dl.y), neg1,
+                                f2_pack(__uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1])))),
+                    d0, d1);
+          f2_unpack(fmul2(f2_pack(p[c][e + 2], p[c][e + 3]),
+                          ffma2(f2_pack(dl.z, dl.w), neg1,
+                                f2_pack(__uint_as_float(dpv[e + 2]), __uint_as_float(dpv[e + 3])))),
+                    d2, d3);
+          dd[e4 * 2] = pack2<kBf16>(d0, d1);
+          dd[e4 * 2 + 1] = pack2<kBf16>(d2, d3);
         }
 #pragma unroll
         for (int w = 0; w < 4; ++w) {

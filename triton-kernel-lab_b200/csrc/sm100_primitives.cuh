@@ -502,6 +502,12 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // Two base-2 exponentials on the FMA pipe with packed arithmetic (about five
 // issued instructions per exponential instead of ten).  Same reduction as
 // exp2_fma — n = round(x) from the low mantissa bits of x + 1.5*2^23,
