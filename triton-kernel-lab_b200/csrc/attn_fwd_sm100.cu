@@ -11,16 +11,20 @@
 // for the P.V product, O = acc / row_sum, and the optional statistic is the
 // base-2 log-sum-exp `row_max + log2(row_sum)` (:254-264).
 //
-// One CTA owns two consecutive 128-row query tiles (A and B) of one
-// (batch, head) and streams the key/value tiles once for both.  12 warps in
-// three warpgroups, registers rebalanced with setmaxnreg:
-//   WG0  warp 0   TMA producer (Q_A and Q_B once, then K and V tiles
+// A work item is two consecutive 128-row query tiles (A and B) of one
+// (batch, head); the CTA streams the key/value tiles once for both.  Large
+// causal problems run one persistent CTA per SM over balanced units of items
+// (the next item's Q load and first products overlap the current epilogue);
+// otherwise one CTA runs one item.  12 warps in three warpgroups, registers
+// rebalanced with setmaxnreg:
+//   WG0  warp 0   TMA producer (Q_A and Q_B per item, then K and V tiles
 //                 through two rings)
 //        warp 1   TMEM allocator and tcgen05.mma issuer (the warp runs the
 //                 loop converged, one elected lane issues)
 //   WG1  warps 4..7   softmax of tile A: thread t owns query row t (TMEM
 //                     lane t); also rescales O_A when its running maximum
-//                     moves, and runs tile A's epilogue
+//                     moves, and runs tile A's epilogue (O_A / row_sum stored
+//                     from registers straight to global memory)
 //   WG2  warps 8..11  the same for tile B
 // Tensor memory (512 columns): O_A, O_B (D columns each), then S_A and S_B
 // (128 columns each).  P is written back as packed 16-bit pairs over the
@@ -43,9 +47,9 @@ struct FwdCfg {
   static constexpr int kKOff = kQOff + 2 * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
-  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2],
-  // p_ready[2], o_final[2]
-  static constexpr int kNumBars = 1 + 4 * kStages + 6;
+  // q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S],
+  // s_full[2], p_ready[2], o_final[2]
+  static constexpr int kNumBars = 2 + 4 * kStages + 6;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -168,12 +172,51 @@ __device__ __forceinline__ void softmax_tile(uint32_t s_addr, int lim, float sca
   m_run = m_use;
 }
 
+// Work is split into units of one or two query-tile pairs ("items"), walked
+// by every CTA with a stride of gridDim.x.  Modes:
+//   kOrderHead   one item per unit, head-major (the pairs of one head are
+//                adjacent, so resident CTAs share a few heads' K/V in L2),
+//                heaviest pair of a head first;
+//   kOrderLpt    one item per unit, heaviest pairs of every head first (when
+//                all heads' K/V fit in L2 together);
+//   kOrderPaired unit u of head bh holds the pairs ct = n_ctiles-1-p and
+//                ct = p, so every causal unit costs the same number of key
+//                tiles and a static stride over units keeps persistent CTAs
+//                balanced.
+// The launcher runs one CTA per unit (hardware scheduling) in the first two
+// modes and one persistent CTA per SM in the third.
+constexpr int kOrderHead = 0;
+constexpr int kOrderLpt = 1;
+constexpr int kOrderPaired = 2;
+
+__device__ __forceinline__ int fwd_unit_items(int u, int n_ctiles, int mode) {
+  if (mode != kOrderPaired) return 1;
+  const int p = u % ((n_ctiles + 1) / 2);
+  return (p == n_ctiles - 1 - p) ? 1 : 2;
+}
+
+__device__ __forceinline__ void fwd_unit_item(int u, int sub, int BH, int n_ctiles, int mode, int& bh, int& ct) {
+  if (mode == kOrderPaired) {
+    const int n_pairs = (n_ctiles + 1) / 2;
+    bh = u / n_pairs;
+    const int p = u % n_pairs;
+    ct = (sub == 0) ? n_ctiles - 1 - p : p;
+  } else if (mode == kOrderLpt) {
+    bh = u % BH;
+    ct = n_ctiles - 1 - u / BH;
+  } else {
+    bh = u / n_ctiles;
+    ct = n_ctiles - 1 - u % n_ctiles;
+  }
+}
+
 template <int D, bool kBf16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    float* __restrict__ lse, int S, int BH, int n_ctiles, int causal, int lpt_order,
-                    float scale_log2, unsigned long long timeout_ns, int* status) {
+                    uint16_t* __restrict__ out, float* __restrict__ lse,
+                    int S, int BH, int n_ctiles, int causal, int mode, int n_units, int d_real, float scale_log2,
+                    unsigned long long timeout_ns, int* status) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -183,27 +226,15 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int wg = warp >> 2;
-  // Grid order.  Head-major (default): the query-tile pairs of one
-  // (batch, head) are adjacent, so the CTAs resident at any time share a few
-  // heads' K/V in L2; within a head the heaviest pairs (largest index under
-  // a causal mask) launch first.  Heaviest-first across all heads
-  // (lpt_order, chosen by the launcher when every head's K/V fits in L2
-  // together): the longest pairs of every head start in the first waves and
-  // the short ones fill the tail.
-  const int bh = lpt_order ? static_cast<int>(blockIdx.x) % BH : static_cast<int>(blockIdx.x) / n_ctiles;
-  const int ct = n_ctiles - 1 - (lpt_order ? static_cast<int>(blockIdx.x) / BH : static_cast<int>(blockIdx.x) % n_ctiles);
-  const int m0 = ct * 2 * kTileRows;
   const int n_ntiles = (S + kTileRows - 1) / kTileRows;
-  // Key tiles per query tile: tile A (index 2 ct) and tile B (2 ct + 1).
-  const int n_kv_a = causal ? min(2 * ct + 1, n_ntiles) : n_ntiles;
-  const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
 
   uint8_t* sQ = smem + C::kQOff;
   uint8_t* sK = smem + C::kKOff;
   uint8_t* sV = smem + C::kVOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_empty = bars + 1;
+  uint64_t* k_full = bars + 2;
   uint64_t* k_empty = k_full + C::kStages;
   uint64_t* v_full = k_empty + C::kStages;
   uint64_t* v_empty = v_full + C::kStages;
@@ -214,6 +245,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < C::kStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -240,29 +272,47 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
 
+  // Every role walks the same item sequence: units blockIdx.x, +gridDim.x,
+  // ...; barrier phases follow running counters (items, key tiles, S and P
+  // tiles per query tile) so consecutive items pipeline into each other.
   if (wg == 0) {
     warpgroup_reg_dec<kFwdRegsCtrl>();
     if (warp == 0 && lane == 0) {
       // ---------------- TMA producer ----------------
-      mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
+      uint32_t g = 0;  // key tiles loaded so far
+      int it = 0;      // items so far
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        const int n_sub = fwd_unit_items(u, n_ctiles, mode);
+        for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
+          int bh, ct;
+          fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
+          const int m0 = ct * 2 * kTileRows;
+          const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
+          // Q_A and Q_B are free once the previous item's last S product
+          // has completed.
+          if (it > 0 && !(ok = mbar_wait(q_empty, (it - 1) & 1, ctl, timeout_ns, status, 13))) break;
+          mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
 #pragma unroll
-      for (int x = 0; x < 2; ++x)
+          for (int x = 0; x < 2; ++x)
 #pragma unroll
-        for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sQ + x * C::kTileBytes + b * kBlockBytes, &tm_q, q_full, b * 64, m0 + x * kTileRows, bh);
-      for (int j = 0; j < n_kv_b; ++j) {
-        const int st = j % C::kStages;
-        const uint32_t ph = (j / C::kStages) & 1;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, ctl, timeout_ns, status, 1)) break;
-        mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
+            for (int b = 0; b < D / 64; ++b)
+              tma_load_3d(sQ + x * C::kTileBytes + b * kBlockBytes, &tm_q, q_full, b * 64, m0 + x * kTileRows, bh);
+          for (int j = 0; j < n_kv_b; ++j, ++g) {
+            const int st = g % C::kStages;
+            const uint32_t ph = (g / C::kStages) & 1;
+            if (!(ok = mbar_wait(&k_empty[st], ph ^ 1, ctl, timeout_ns, status, 1))) break;
+            mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
 #pragma unroll
-        for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sK + st * C::kTileBytes + b * kBlockBytes, &tm_k, &k_full[st], b * 64, j * kTileRows, bh);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, ctl, timeout_ns, status, 2)) break;
-        mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
+            for (int b = 0; b < D / 64; ++b)
+              tma_load_3d(sK + st * C::kTileBytes + b * kBlockBytes, &tm_k, &k_full[st], b * 64, j * kTileRows, bh);
+            if (!(ok = mbar_wait(&v_empty[st], ph ^ 1, ctl, timeout_ns, status, 2))) break;
+            mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
 #pragma unroll
-        for (int b = 0; b < D / 64; ++b)
-          tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
+            for (int b = 0; b < D / 64; ++b)
+              tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
+          }
+        }
       }
     } else if (warp == 1) {
       // ---------------- MMA issuer ----------------
@@ -277,9 +327,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(sK));
       const uint32_t v_lo0 = sdesc_lo_mnmajor(smem_u32(sV), kTileRows);
       constexpr uint32_t kTileLo = C::kTileBytes >> 4;  // low-word step between tiles
-      auto issue_s = [&](int x, int j) {
+      auto issue_s = [&](int x, int st) {
         const uint32_t q_lo = q_lo0 + x * kTileLo;
-        const uint32_t k_lo = k_lo0 + (j % C::kStages) * kTileLo;
+        const uint32_t k_lo = k_lo0 + st * kTileLo;
         const uint32_t d = tmem + C::kColS0 + 128u * x;
         if (leader) {
 #pragma unroll
@@ -290,11 +340,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         __syncwarp();
       };
-      auto issue_pv = [&](int x, int j) {
-        const uint32_t v_lo = v_lo0 + (j % C::kStages) * kTileLo;
+      auto issue_pv = [&](int x, int st, bool accumulate) {
+        const uint32_t v_lo = v_lo0 + st * kTileLo;
         const uint32_t p_col = tmem + C::kColS0 + 128u * x;
         const uint32_t d = tmem + C::kColO0 + D * x;
-        const uint32_t acc0 = j > 0 ? 1u : 0u;
+        const uint32_t acc0 = accumulate ? 1u : 0u;
         if (leader) {
 #pragma unroll
           for (int kk = 0; kk < kTileRows / 16; ++kk)
@@ -306,46 +356,70 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (leader) umma_commit(bar);
         __syncwarp();
       };
-      bool ok = warp_wait(q_full, 0, ctl, timeout_ns, status, 3);
-      if (ok) ok = warp_wait(&k_full[0], 0, ctl, timeout_ns, status, 4);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        commit(&k_empty[0]);
-      }
-      for (int j = 0; ok && j < n_kv_b; ++j) {
-        const int st = j % C::kStages;
-        const uint32_t ph = (j / C::kStages) & 1;
-        const int j1 = j + 1;
-        const int st1 = j1 % C::kStages;
-        const uint32_t ph1 = (j1 / C::kStages) & 1;
-        bool v_ready = false, k_ready = false;
-        if (j < n_kv_a) {
-          if (!(ok = warp_wait(&p_ready[0], j & 1, ctl, timeout_ns, status, 5))) break;
-          if (!(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 6))) break;
-          v_ready = true;
-          tc_fence_after();
-          issue_pv(0, j);
-          if (j1 < n_kv_a) {
-            if (!(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
-            k_ready = true;
-            issue_s(0, j1);
-          } else {
-            commit(&o_final[0]);
+      uint32_t g = 0;             // key tiles consumed so far
+      uint32_t pa = 0, pb = 0;    // P tiles of A / B consumed so far
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        const int n_sub = fwd_unit_items(u, n_ctiles, mode);
+        for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
+          int bh, ct;
+          fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
+          const int n_kv_a = causal ? min(2 * ct + 1, n_ntiles) : n_ntiles;
+          const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
+          // S_x(0) overwrites the previous item's P_x, whose P.V was issued
+          // earlier on this thread: the tensor pipe keeps that order.
+          if (!(ok = warp_wait(q_full, it & 1, ctl, timeout_ns, status, 3))) break;
+          {
+            const int st0 = g % C::kStages;
+            if (!(ok = warp_wait(&k_full[st0], (g / C::kStages) & 1, ctl, timeout_ns, status, 4))) break;
+            tc_fence_after();
+            issue_s(0, st0);
+            issue_s(1, st0);
+            commit(&k_empty[st0]);
+            if (n_kv_b == 1) commit(q_empty);
           }
-        }
-        if (!(ok = warp_wait(&p_ready[1], j & 1, ctl, timeout_ns, status, 8))) break;
-        if (!v_ready && !(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
-        tc_fence_after();
-        issue_pv(1, j);
-        commit(&v_empty[st]);
-        if (j1 < n_kv_b) {
-          if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
-          issue_s(1, j1);
-          commit(&k_empty[st1]);
-        } else {
-          commit(&o_final[1]);
+          for (int j = 0; ok && j < n_kv_b; ++j) {
+            const uint32_t gj = g + j, gj1 = gj + 1;
+            const int st = gj % C::kStages;
+            const uint32_t ph = (gj / C::kStages) & 1;
+            const int st1 = gj1 % C::kStages;
+            const uint32_t ph1 = (gj1 / C::kStages) & 1;
+            const int j1 = j + 1;
+            bool v_ready = false, k_ready = false;
+            if (j < n_kv_a) {
+              // P_A(j) ready also means tile A's warps finished reading the
+              // previous item's O_A (the epilogue precedes it).
+              if (!(ok = warp_wait(&p_ready[0], pa & 1, ctl, timeout_ns, status, 5))) break;
+              ++pa;
+              if (!(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 6))) break;
+              v_ready = true;
+              tc_fence_after();
+              issue_pv(0, st, j > 0);
+              if (j1 < n_kv_a) {
+                if (!(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
+                k_ready = true;
+                issue_s(0, st1);
+              } else {
+                commit(&o_final[0]);
+              }
+            }
+            if (!(ok = warp_wait(&p_ready[1], pb & 1, ctl, timeout_ns, status, 8))) break;
+            ++pb;
+            if (!v_ready && !(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
+            tc_fence_after();
+            issue_pv(1, st, j > 0);
+            commit(&v_empty[st]);
+            if (j1 < n_kv_b) {
+              if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
+              issue_s(1, st1);
+              commit(&k_empty[st1]);
+              if (j1 == n_kv_b - 1) commit(q_empty);  // the item's last S product
+            } else {
+              commit(&o_final[1]);
+            }
+          }
+          g += n_kv_b;
         }
       }
     }
@@ -355,79 +429,130 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const int x = wg - 1;
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
-    const int row_g = m0 + x * kTileRows + r;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
     const uint32_t s_addr = t_lane + C::kColS0 + 128u * x;
     const uint32_t o_addr = t_lane + C::kColO0 + D * x;
-    float m_run = -INFINITY, l_run = 0.0f;
+    // 32-byte stores when every row starts on a 32-byte boundary.
+    const bool wide_store = (d_real % 16) == 0 && (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
+    uint32_t cs = 0;  // S tiles of this query tile consumed so far
+    int it = 0;
     bool ok = true;
-    const int n_kv_x = (x == 0) ? n_kv_a : n_kv_b;
-    for (int j = 0; j < n_kv_x; ++j) {
-      if (!(ok = warp_wait(&s_full[x], j & 1, ctl, timeout_ns, status, 11))) break;
-      tc_fence_after();
-      const int n0 = j * kTileRows;
-      int lim = S - n0;
-      if (causal) lim = min(lim, row_g - n0 + 1);
-      float alpha;
-      bool need;
-      if (__any_sync(0xffffffffu, lim < kTileRows))
-        softmax_tile<kBf16, true>(s_addr, lim, scale_log2, m_run, l_run, alpha, need);
-      else
-        softmax_tile<kBf16, false>(s_addr, lim, scale_log2, m_run, l_run, alpha, need);
-      // S_x(j) completing implies P_x(j-1).V has completed, so O_x can be
-      // rescaled here, before P_x(j) is released to the MMA warp.
-      if (j >= 1 && __any_sync(0xffffffffu, need)) {
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+      const int n_sub = fwd_unit_items(u, n_ctiles, mode);
+      for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
+        int bh, ct;
+        fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
+        const int m0 = ct * 2 * kTileRows;
+        const int row_g = m0 + x * kTileRows + r;
+        const int n_kv_x = causal ? min(2 * ct + 1 + x, n_ntiles) : n_ntiles;
+        float m_run = -INFINITY, l_run = 0.0f;
+        for (int j = 0; j < n_kv_x; ++j, ++cs) {
+          if (!(ok = warp_wait(&s_full[x], cs & 1, ctl, timeout_ns, status, 11))) break;
+          tc_fence_after();
+          const int n0 = j * kTileRows;
+          int lim = S - n0;
+          if (causal) lim = min(lim, row_g - n0 + 1);
+          float alpha;
+          bool need;
+          if (__any_sync(0xffffffffu, lim < kTileRows))
+            softmax_tile<kBf16, true>(s_addr, lim, scale_log2, m_run, l_run, alpha, need);
+          else
+            softmax_tile<kBf16, false>(s_addr, lim, scale_log2, m_run, l_run, alpha, need);
+          // S_x(j) completing implies P_x(j-1).V has completed, so O_x can be
+          // rescaled here, before P_x(j) is released to the MMA warp.
+          if (j >= 1 && __any_sync(0xffffffffu, need)) {
 #pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + cb * 32, o);
-          tmem_wait_ld();
-          reg_fence(o);
+            for (int cb = 0; cb < D / 32; ++cb) {
+              uint32_t o[32];
+              tmem_ld32(o_addr + cb * 32, o);
+              tmem_wait_ld();
+              reg_fence(o);
 #pragma unroll
-          for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-          tmem_st32(o_addr + cb * 32, o);
+              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+              tmem_st32(o_addr + cb * 32, o);
+            }
+          }
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_ready[x]);
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[x]);
-    }
-    uint8_t* stage = sQ + x * C::kTileBytes;  // Q_x is dead once O_x is final
-    if (ok) ok = warp_wait(&o_final[x], 0, ctl, timeout_ns, status, 12);
-    if (ok) {
-      tc_fence_after();
-      const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+        // Epilogue.  The next item's P_x(0) is released only after the O_x
+        // loads below, which keeps the MMA warp from overwriting O_x early.
+        // ok is warp-uniform; after a failed wait the epilogue is skipped
+        // but the warpgroup barrier below is still reached.
+        if (ok) ok = warp_wait(&o_final[x], it & 1, ctl, timeout_ns, status, 12);
+        if (ok) tc_fence_after();
+        const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+        const bool row_ok = row_g < S;
+        if (mode != kOrderPaired) {
+          // One item per CTA: O_x / row_sum staged through Q_x (dead once O_x
+          // is final) and written by one TMA store, which clips rows past S
+          // and columns past the true head_dim.
+          uint8_t* stage = sQ + x * C::kTileBytes;
 #pragma unroll
-      for (int cb = 0; cb < D / 32; ++cb) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + cb * 32, o);
-        tmem_wait_ld();
-        reg_fence(o);
+          for (int cb = 0; ok && cb < D / 32; ++cb) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + cb * 32, o);
+            tmem_wait_ld();
+            reg_fence(o);
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint4 w;
-          w.x = pack2<kBf16>(__uint_as_float(o[ch * 8 + 0]) * inv_l, __uint_as_float(o[ch * 8 + 1]) * inv_l);
-          w.y = pack2<kBf16>(__uint_as_float(o[ch * 8 + 2]) * inv_l, __uint_as_float(o[ch * 8 + 3]) * inv_l);
-          w.z = pack2<kBf16>(__uint_as_float(o[ch * 8 + 4]) * inv_l, __uint_as_float(o[ch * 8 + 5]) * inv_l);
-          w.w = pack2<kBf16>(__uint_as_float(o[ch * 8 + 6]) * inv_l, __uint_as_float(o[ch * 8 + 7]) * inv_l);
-          *reinterpret_cast<uint4*>(stage + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
+            for (int ch = 0; ch < 4; ++ch) {
+              uint4 w;
+              w.x = pack2<kBf16>(__uint_as_float(o[ch * 8 + 0]) * inv_l, __uint_as_float(o[ch * 8 + 1]) * inv_l);
+              w.y = pack2<kBf16>(__uint_as_float(o[ch * 8 + 2]) * inv_l, __uint_as_float(o[ch * 8 + 3]) * inv_l);
+              w.z = pack2<kBf16>(__uint_as_float(o[ch * 8 + 4]) * inv_l, __uint_as_float(o[ch * 8 + 5]) * inv_l);
+              w.w = pack2<kBf16>(__uint_as_float(o[ch * 8 + 6]) * inv_l, __uint_as_float(o[ch * 8 + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(stage + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
+            }
+          }
+          fence_proxy_async_smem();
+          // Every warp of the warpgroup reaches this barrier exactly once
+          // (one item per CTA in this mode), on failure too.
+          named_barrier_sync(1 + x, 128);
+          // (Tile B of a short sequence may lie wholly past S: nothing to store.)
+          if (ok && q4 == 0 && lane == 0 && !ctl->abort && m0 + x * kTileRows < S) {
+#pragma unroll
+            for (int b = 0; b < D / 64; ++b)
+              tma_store_3d(&tm_o, stage + b * kBlockBytes, b * 64, m0 + x * kTileRows, bh);
+            tma_store_commit();
+            tma_store_wait_read_all();
+          }
+        } else {
+          // Persistent CTAs: Q_x is already loading the next item, so O_x /
+          // row_sum goes from registers straight to global memory, one row
+          // per thread (rows past S, columns past the true head_dim skipped).
+          uint16_t* orow = out + (static_cast<size_t>(bh) * S + row_g) * d_real;
+#pragma unroll
+          for (int cb = 0; ok && cb < D / 32; ++cb) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + cb * 32, o);
+            tmem_wait_ld();
+            reg_fence(o);
+            uint32_t w[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e)
+              w[e] = pack2<kBf16>(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+            if (row_ok) {
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh) {
+                const int col = cb * 32 + hh * 16;
+                if (wide_store && col < d_real) {
+                  st_global_v8(orow + col, &w[hh * 8]);
+                } else if (!wide_store) {
+#pragma unroll
+                  for (int q = 0; q < 2; ++q)
+                    if (col + q * 8 < d_real)
+                      *reinterpret_cast<uint4*>(orow + col + q * 8) = make_uint4(
+                          w[hh * 8 + q * 4], w[hh * 8 + q * 4 + 1], w[hh * 8 + q * 4 + 2], w[hh * 8 + q * 4 + 3]);
+                }
+              }
+            }
+          }
         }
+        if (ok && lse != nullptr && row_ok) lse[static_cast<size_t>(bh) * S + row_g] = m_run + lg2(l_run);
       }
-      fence_proxy_async_smem();
     }
-    // Every warp of the warpgroup reaches this barrier exactly once.
-    named_barrier_sync(1 + x, 128);
-    // (Tile B of a short sequence may lie wholly past S: nothing to store.)
-    if (q4 == 0 && lane == 0 && !ctl->abort && m0 + x * kTileRows < S) {
-#pragma unroll
-      for (int b = 0; b < D / 64; ++b)
-        tma_store_3d(&tm_o, stage + b * kBlockBytes, b * 64, m0 + x * kTileRows, bh);
-      tma_store_commit();
-      tma_store_wait_read_all();
-    }
-    if (ok && lse != nullptr && row_g < S)
-      lse[static_cast<size_t>(bh) * S + row_g] = m_run + lg2(l_run);
   }
 
   tc_fence_before();
@@ -445,9 +570,11 @@ int launch_fwd_t(const FwdArgs& a) {
   static_assert(C::kSmemBytes <= 232448, "forward shared memory exceeds the sm_100 limit");
   auto kern = attn_fwd_kernel<D, kBf16>;
   static bool attr_set[64] = {};
+  static int sm_count[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
+  if (dev >= 64) return kErrLaunch;
+  if (!attr_set[dev]) {
     // The setmaxnreg split inside the kernel assumes exactly kFwdLaunchRegs
     // registers per thread at launch; refuse to run a build that differs.
     cudaFuncAttributes attr;
@@ -456,17 +583,37 @@ int launch_fwd_t(const FwdArgs& a) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
         cudaSuccess)
       return kErrLaunch;
+    if (cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sm_count[dev] <= 0)
+      return kErrLaunch;
     attr_set[dev] = true;
   }
   const int n_ctiles = static_cast<int>((a.S + 2 * kTileRows - 1) / (2 * kTileRows));
-  const long long grid = static_cast<long long>(n_ctiles) * a.BH;
-  // Heaviest-first order only pays when it cannot thrash L2: K and V of all
-  // heads together must stay well inside the 126 MB L2.
-  const double kv_bytes = 2.0 * static_cast<double>(a.BH) * static_cast<double>(a.S) * D * 2.0;
-  const int lpt_order = (a.causal && kv_bytes <= 80.0e6) ? 1 : 0;
+  const long long n_items = static_cast<long long>(n_ctiles) * a.BH;
+  const long long n_pair_units = static_cast<long long>((n_ctiles + 1) / 2) * a.BH;
+  int mode;
+  long long n_units, grid;
+  if (a.causal && n_ctiles > 1 && n_pair_units >= 2LL * sm_count[dev]) {
+    // Persistent: one CTA per SM walks equal-cost paired units, so the next
+    // item's Q load and first products overlap the current epilogue; at
+    // least two units per SM keep the last round's imbalance small.
+    mode = kOrderPaired;
+    n_units = n_pair_units;
+    grid = sm_count[dev];
+  } else {
+    // One CTA per item, scheduled by the hardware.  Heaviest-first across
+    // heads only pays when it cannot thrash L2: K and V of all heads
+    // together must stay well inside the 126 MB L2.
+    const double kv_bytes = 2.0 * static_cast<double>(a.BH) * static_cast<double>(a.S) * D * 2.0;
+    mode = (a.causal && kv_bytes <= 80.0e6) ? kOrderLpt : kOrderHead;
+    n_units = n_items;
+    grid = n_items;
+  }
+  if (n_units > INT32_MAX || grid > INT32_MAX) return kErrTooLarge;
   kern<<<static_cast<unsigned>(grid), kFwdThreads, C::kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), static_cast<int>(a.BH), n_ctiles,
-      a.causal, lpt_order, a.scale_log2, a.timeout_ns, a.status);
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, static_cast<uint16_t*>(a.o), a.lse, static_cast<int>(a.S),
+      static_cast<int>(a.BH), n_ctiles, a.causal, mode, static_cast<int>(n_units), static_cast<int>(a.D),
+      a.scale_log2, a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 

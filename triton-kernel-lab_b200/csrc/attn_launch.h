@@ -13,6 +13,7 @@ struct FwdArgs {
   const CUtensorMap* tm_k;
   const CUtensorMap* tm_v;
   const CUtensorMap* tm_o;
+  void* o;     // output, (B*H, S, D) 16-bit (persistent mode stores it directly)
   float* lse;  // nullptr: do not store the statistic
   int64_t BH, S, D;
   bool bf16;

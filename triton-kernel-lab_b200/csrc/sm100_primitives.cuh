@@ -532,6 +532,14 @@ __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& p0, flo
   p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
+// 32-byte global store of eight 32-bit words (sm_100 st.global.v8); `dst`
+// must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
 // Three-input maximum (sm_100 max.f32 with three sources).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
