@@ -120,6 +120,15 @@ __device__ __forceinline__ void stage_row(uint32_t t_row, uint8_t* tile, int r, 
 // is one packed fma.  kMasked adds the causal diagonal (query q0+e is dropped
 // when it precedes this thread's key, diag_key) and the ragged key tail
 // (key_ok false: the whole row is zero).
+// Of the 16 exponential pairs of an unmasked 32-query chunk, the pairs of
+// this many 4-query groups (two pairs each) run on the FMA pipe
+// (exp2_fma_pair): with both dS warpgroups in their P phase the MUFU
+// (16 exp2/clk/SM) would otherwise bound it.
+#ifndef TK_BWD_EMU_GROUPS_PER8
+#define TK_BWD_EMU_GROUPS_PER8 3
+#endif
+constexpr int kBwdEmuGroupsPer8 = TK_BWD_EMU_GROUPS_PER8;
+
 template <bool kMasked>
 __device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const float* nlse_s, float scale_log2,
                                             int q0, int diag_key, bool key_ok, float (&p)[32]) {
@@ -134,14 +143,20 @@ __device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const floa
               x[1]);
     f2_unpack(ffma2(f2_pack(__uint_as_float(sv[e0 + 2]), __uint_as_float(sv[e0 + 3])), scale2, f2_pack(l.z, l.w)),
               x[2], x[3]);
+    if (!kMasked && e4 >= 8 - kBwdEmuGroupsPer8) {
+      // Unmasked: every argument is finite (LSE of a real row bounds it).
+      exp2_fma_pair(x[0], x[1], p[e0], p[e0 + 1]);
+      exp2_fma_pair(x[2], x[3], p[e0 + 2], p[e0 + 3]);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = e0 + j;
-      float pv = ex2(x[j]);
-      if constexpr (kMasked) {
-        if (q0 + e < diag_key || !key_ok) pv = 0.0f;
+      for (int j = 0; j < 4; ++j) {
+        const int e = e0 + j;
+        float pv = ex2(x[j]);
+        if constexpr (kMasked) {
+          if (q0 + e < diag_key || !key_ok) pv = 0.0f;
+        }
+        p[e] = pv;
       }
-      p[e] = pv;
     }
   }
 }
