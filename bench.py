@@ -41,10 +41,11 @@ CONFIGS = {
 }
 L2_FLUSH_BYTES = 256 << 20
 # DRAM bytes (read + write) per (batch, head) slab of the C3 shape for one
-# launch of the fused backward kernel, from ncu (dram__bytes_read.sum +
-# dram__bytes_write.sum) on 64 slabs (profiles/attn_kernels_c3_bh64.md):
-# 631.3 MB / 64.  Traffic grows in proportion to the slab count.
-BWD_DRAM_BYTES_PER_SLAB_C3 = 631.26e6 / 64
+# launch of the fused backward kernel, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of the 64-slab case:
+# 404.8 MB + 223.9 MB over 64 slabs.  Traffic grows in proportion to the
+# slab count.
+BWD_DRAM_BYTES_PER_SLAB_C3 = 628.68e6 / 64
 THROTTLE_REASONS = {
     0x1: "gpu_idle",
     0x2: "applications_clocks_setting",
