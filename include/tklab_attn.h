@@ -135,6 +135,32 @@ TK_API int tk_attn_bwd_deterministic(const void* q, const void* k, const void* v
                                      void* dv, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                                      int dtype, int causal, float scale, void* stream);
 
+/* Rotate-half RoPE fused into the attention (the reference applies it as a
+ * separate op, `rope` in src/tklab/kernels/rope.py:310-316, whose kernels
+ * :27-160 fix the arithmetic; this is the step before attention).  Tables
+ * cos and sin are (seq, head_dim/2) fp32, indexed by the position only and
+ * shared by every batch and head; head_dim must be 64 or 128.
+ *   tk_attn_fwd_rope        o = attention(R q, R k, v): the forward kernel
+ *                           rotates each Q and K tile in shared memory after
+ *                           its load (rotated values rounded to dtype, as the
+ *                           reference's separate rope output is); lse as in
+ *                           tk_attn_fwd
+ *   tk_rope_rotate          out = R x (transpose: R^T x) for a contiguous
+ *                           (batch, heads, seq, head_dim) tensor; out may be x.
+ *                           The backward runs tk_attn_bwd_pre and
+ *                           tk_attn_bwd_fused on R q, R k, then
+ *   tk_attn_dq_convert_rope dq = R^T dq_accum rounded to dtype (in place of
+ *                           tk_attn_dq_convert), and tk_rope_rotate with
+ *                           transpose on dk. */
+TK_API int tk_attn_fwd_rope(const void* q, const void* k, const void* v, const float* cos, const float* sin,
+                            void* o, float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                            int dtype, int causal, float scale, void* stream);
+TK_API int tk_rope_rotate(const void* x, void* out, const float* cos, const float* sin, int64_t batch,
+                          int64_t heads, int64_t seq, int64_t head_dim, int dtype, int transpose, void* stream);
+TK_API int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float* cos, const float* sin,
+                                   int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
+                                   void* stream);
+
 /* Bytes of the fp32 dQ accumulator tk_attn_bwd needs (0 on bad sizes). */
 TK_API size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);
 

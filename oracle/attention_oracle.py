@@ -24,6 +24,12 @@ the triton-kernel-lab project):
   for their products (``:368-533``).  Pure numpy loops over tiles: for small
   cases only.
 
+* ``rope_rotate`` / ``rope_attention_forward`` / ``rope_attention_backward``
+  — rotate-half RoPE in fp32 rounded to the element type
+  (``src/tklab/kernels/rope.py:27-74``; the transpose of ``:77-160``) and the
+  reference's two-op pipeline rope → attention with its chain rule, for the
+  fused RoPE attention.
+
 Parity is pinned: ``tests/test_oracle_golden.py`` checks all three against
 golden vectors produced by the reference's own Triton kernels (run under the
 Triton CPU interpreter) and its SDPA/manual references, committed under
@@ -269,3 +275,48 @@ def chunked_reference(
         dq[..., m0:m1, :] = (dscores @ kf) * scale
         dk += (dscores.transpose(-2, -1) @ qf[..., m0:m1, :]) * scale
     return out, lse, dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# Rotate-half RoPE (reference src/tklab/kernels/rope.py:27-74 forward,
+# :77-160 backward = transpose rotation) and the rope -> attention pipeline.
+# ---------------------------------------------------------------------------
+def rope_rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *, transpose: bool = False) -> torch.Tensor:
+    """R x (or R^T x) over the last dim in fp32, rounded to x's dtype.
+
+    ``cos``/``sin`` are (seq, dim/2) tables broadcast over the leading dims
+    of ``x`` (positions along dim -2), as the fused kernel indexes them.
+    """
+    xf = x.float()
+    half = xf.shape[-1] // 2
+    first, second = xf[..., :half], xf[..., half:]
+    c, s = cos.float(), sin.float()
+    if transpose:
+        s = -s
+    out = torch.cat((first * c - second * s, second * c + first * s), dim=-1)
+    return out.to(x.dtype)
+
+
+def rope_attention_forward(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, *, causal: bool
+) -> torch.Tensor:
+    """fp32 attention of the dtype-rounded rotated Q and K (the reference's rope output feeds attention)."""
+    return sdpa_forward(rope_rotate(q, cos, sin), rope_rotate(k, cos, sin), v, causal=causal)
+
+
+def rope_attention_backward(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    do: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    *,
+    causal: bool,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """fp32 gradients: manual attention algebra on (R q, R k), then R^T on dQ and dK."""
+    q_r, k_r = rope_rotate(q, cos, sin), rope_rotate(k, cos, sin)
+    dq_r, dk, dv = manual_backward(q_r, k_r, v, do, causal=causal)
+    dq = rope_rotate(dq_r, cos, sin, transpose=True)
+    dk = rope_rotate(dk, cos, sin, transpose=True)
+    return dq, dk, dv

@@ -25,9 +25,10 @@ def pytest_configure(config: pytest.Config) -> None:
     config.addinivalue_line("markers", "gpu: requires a CUDA GPU (B200, sm_100a)")
 
 
-def golden_cases() -> list[str]:
-    """Names of the committed golden fixtures."""
-    return sorted(path.stem for path in GOLDEN_DIR.glob("*.npz"))
+def golden_cases(*, rope: bool = False) -> list[str]:
+    """Names of the committed golden fixtures: plain attention, or (``rope``) the fused-RoPE cases."""
+    names = sorted(path.stem for path in GOLDEN_DIR.glob("*.npz"))
+    return [name for name in names if name.startswith("rope_") == rope]
 
 
 def load_golden(name: str) -> dict[str, object]:

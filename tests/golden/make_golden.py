@@ -14,6 +14,14 @@ For every case it draws seeded inputs on the CPU and records:
   (fp32 ``F.scaled_dot_product_attention``) and its autograd gradient;
 * ``man_dq``/``man_dk``/``man_dv`` — ``_manual_fp32_backward`` from the
   reference's ``tests/test_flash_attention_backward.py``.
+RoPE attention cases (``rope_*``) add the reference's rotate-half kernels
+(``src/tklab/kernels/rope.py`` ``_rope_forward_kernel`` /
+``_rope_backward_kernel``, interpreter, fp16 tables, one (batch, head) slab
+at a time): ``ref_qrot``/``ref_krot`` (rope of Q and K), the attention
+kernels above on the rotated tensors (``ref_o``, ``ref_lse``, ``ref_dv``),
+dQ and dK mapped back through the rope backward kernel (``ref_dq``,
+``ref_dk``), and the same chain with the fp32 manual algebra
+(``man_dq``/``man_dk``/``man_dv``).
 16-bit tensors are stored as their raw uint16 bit patterns (``<name>_bits``)
 with the dtype name, so tests rebuild bit-identical tensors; fp32 tensors are
 stored as float32.  The fp32 config-1 case keeps the SDPA gradients (its
@@ -45,6 +53,75 @@ CASES = [
     ("bf16_s130_d128_causal", (1, 2, 130, 128), "bfloat16", True, 5, False),
     ("bf16_s300_d128_noncausal", (1, 1, 300, 128), "bfloat16", False, 6, False),
 ]
+
+
+# (name, shape, dtype, causal, seed): fused-RoPE attention cases.
+ROPE_CASES = [
+    ("rope_f16_s129_d64_causal", (1, 2, 129, 64), "float16", True, 11),
+    ("rope_f16_s200_d64_noncausal", (2, 1, 200, 64), "float16", False, 12),
+]
+
+
+def _rope_tables(torch, seq: int, dim: int, dtype):
+    """angle[p][i] = p * 10000^(-2i/dim), evaluated in float64."""
+    inv = 10000.0 ** (-torch.arange(0, dim // 2, dtype=torch.float64) * 2.0 / dim)
+    angles = torch.arange(seq, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cos(angles).to(dtype), torch.sin(angles).to(dtype)
+
+
+def _ref_rope(torch, triton, rp, x, cos, sin, *, backward_of=None):
+    """Reference rope over the last dim of (b, h, s, d), one slab at a time.
+
+    With ``backward_of`` (the rope input), ``x`` is the upstream gradient and
+    the result is the rope input gradient (the transpose rotation)."""
+    b, h, s, d = x.shape
+    out = torch.empty_like(x)
+    grid = (s, triton.cdiv(d // 2, rp._BLOCK_SIZE))
+    for i in range(b):
+        for j in range(h):
+            src = x[i, j].contiguous()
+            dst = torch.empty_like(src)
+            if backward_of is None:
+                rp._rope_forward_kernel[grid](
+                    src, cos, sin, dst, src.stride(0), cos.stride(0), sin.stride(0), dst.stride(0), d // 2,
+                    BLOCK_SIZE=rp._BLOCK_SIZE,
+                )
+            else:
+                xin = backward_of[i, j].contiguous()
+                rp._rope_backward_kernel[grid](
+                    src, xin, cos, sin, dst, dst, dst, src.stride(0), xin.stride(0), cos.stride(0),
+                    sin.stride(0), dst.stride(0), dst.stride(0), dst.stride(0), d // 2,
+                    COMPUTE_DCOS=False, COMPUTE_DSIN=False, BLOCK_SIZE=rp._BLOCK_SIZE,
+                )
+            out[i, j] = dst
+    return out
+
+
+def _rope_case(torch, triton, fa, rp, ref_tests, shape, dtype_name, causal, seed):
+    dtype = getattr(torch, dtype_name)
+    gen = torch.Generator().manual_seed(seed)
+    q, k, v, do = (torch.randn(shape, generator=gen).to(dtype) for _ in range(4))
+    cos, sin = _rope_tables(torch, shape[2], shape[3], dtype)
+    record = {"dtype": np.array(dtype_name), "causal": np.array(causal), "seed": np.array(seed)}
+    for key, tensor in (("q", q), ("k", k), ("v", v), ("do", do), ("cos", cos), ("sin", sin)):
+        _store(record, key, tensor)
+    q_r = _ref_rope(torch, triton, rp, q, cos, sin)
+    k_r = _ref_rope(torch, triton, rp, k, cos, sin)
+    _store(record, "ref_qrot", q_r)
+    _store(record, "ref_krot", k_r)
+    o, lse, dq_r, dk_r, dv = _reference_kernels(torch, triton, fa, q_r, k_r, v, do, causal)
+    dq = _ref_rope(torch, triton, rp, dq_r, cos, sin, backward_of=q)
+    dk = _ref_rope(torch, triton, rp, dk_r, cos, sin, backward_of=k)
+    record["ref_lse"] = lse.numpy()
+    for key, tensor in (("ref_o", o), ("ref_dq", dq), ("ref_dk", dk), ("ref_dv", dv)):
+        _store(record, key, tensor)
+    man_dq_r, man_dk_r, man_dv = ref_tests._manual_fp32_backward(q_r, k_r, v, do, causal=causal)
+    cos32, sin32 = cos.float(), sin.float()
+    man_dq = _ref_rope(torch, triton, rp, man_dq_r.float(), cos32, sin32, backward_of=q.float())
+    man_dk = _ref_rope(torch, triton, rp, man_dk_r.float(), cos32, sin32, backward_of=k.float())
+    for key, grad in (("man_dq", man_dq), ("man_dk", man_dk), ("man_dv", man_dv)):
+        record[key] = grad.float().numpy()
+    return record
 
 
 def _inputs(torch, shape, dtype_name, seed, c1: bool):
@@ -107,6 +184,7 @@ def main() -> None:
     import torch
     import triton
     from tklab.kernels import flash_attention as fa
+    from tklab.kernels import rope as rp
 
     spec = importlib.util.spec_from_file_location(
         "ref_test_backward", args.reference / "tests" / "test_flash_attention_backward.py"
@@ -136,6 +214,11 @@ def main() -> None:
             record["ref_lse"] = lse.numpy()
             for key, tensor in (("ref_o", o), ("ref_dq", dq), ("ref_dk", dk), ("ref_dv", dv)):
                 _store(record, key, tensor)
+        np.savez_compressed(HERE / f"{name}.npz", **record)
+        print(f"wrote {name}.npz")
+
+    for name, shape, dtype_name, causal, seed in ROPE_CASES:
+        record = _rope_case(torch, triton, fa, rp, ref_tests, shape, dtype_name, causal, seed)
         np.savez_compressed(HERE / f"{name}.npz", **record)
         print(f"wrote {name}.npz")
 

@@ -79,3 +79,45 @@ def test_chunked_reference_matches_manual_algebra() -> None:
         assert relative_frobenius_error(lse, lse_man) < 1e-5
         for got, want in zip((dq, dk, dv), grads, strict=True):
             assert relative_frobenius_error(got, want) < 1e-5
+
+
+ROPE_CASES = golden_cases(rope=True)
+
+
+def test_rope_fixture_set() -> None:
+    assert ROPE_CASES == ["rope_f16_s129_d64_causal", "rope_f16_s200_d64_noncausal"]
+
+
+@pytest.mark.parametrize("name", ROPE_CASES)
+def test_rope_oracle_matches_reference_rope_kernel(name: str) -> None:
+    """rope_rotate reproduces the reference rotate-half kernel's fp16 output.
+
+    Both evaluate x1*c - x2*s / x2*c + x1*s in fp32 and round to fp16; the
+    only freedom is whether the products are fused, which can move a result
+    by one fp16 ulp on rare ties.
+    """
+    case = load_golden(name)
+    cos, sin = case["cos"].float(), case["sin"].float()
+    for src, key in (("q", "ref_qrot"), ("k", "ref_krot")):
+        got = orc.rope_rotate(case[src], cos, sin)
+        want = case[key]
+        assert got.dtype == want.dtype == torch.float16
+        bits_got = got.view(torch.int16).int()
+        bits_want = want.view(torch.int16).int()
+        ulp = (bits_got - bits_want).abs()
+        assert int(ulp.max()) <= 1
+        assert float((ulp > 0).float().mean()) < 1e-3
+
+
+@pytest.mark.parametrize("name", ROPE_CASES)
+def test_rope_attention_oracle_matches_reference_chain(name: str) -> None:
+    """Oracle gradients of attention(R q, R k, v) equal the reference's rope -> attention chain in fp32."""
+    case = load_golden(name)
+    cos, sin = case["cos"].float(), case["sin"].float()
+    dq, dk, dv = orc.rope_attention_backward(
+        case["q"], case["k"], case["v"], case["do"], cos, sin, causal=case["causal"]
+    )
+    for got, key in ((dq, "man_dq"), (dk, "man_dk"), (dv, "man_dv")):
+        assert relative_frobenius_error(got, case[key]) < 1e-5, key
+    o = orc.rope_attention_forward(case["q"], case["k"], case["v"], cos, sin, causal=case["causal"])
+    assert relative_frobenius_error(o, case["ref_o"]) < 2e-3

@@ -45,7 +45,12 @@ def _memory_spec(**overrides: object) -> KernelSpec:
 
 
 def test_registry_contains_the_attention_entries() -> None:
-    assert set(REGISTRY) == {"attention_causal", "attention_noncausal"}
+    assert set(REGISTRY) == {
+        "attention_causal",
+        "attention_noncausal",
+        "attention_rope_causal",
+        "attention_rope_noncausal",
+    }
     for spec in REGISTRY.values():
         assert spec.bound == "compute"
         assert spec.compute_mode == "attention_fp16_fp32acc"

@@ -177,6 +177,53 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   return tk::launch_attn_bwd(a);
 }
 
+int tk_attn_fwd_rope(const void* q, const void* k, const void* v, const float* cos, const float* sin, void* o,
+                     float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
+                     int causal, float scale, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || cos == nullptr || sin == nullptr)
+    return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(cos) || !aligned16(sin))
+    return tk::kErrMisaligned;
+  if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u)) return tk::kErrMisaligned;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  const int64_t bh = batch * heads;
+  CUtensorMap mq, mk, mv, mo;
+  if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mo, o, bh, seq, head_dim, dtype)) return rc;
+  tk::FwdArgs a{&mq, &mk, &mv, &mo, o, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16,
+                causal ? 1 : 0, scale * kLog2e, g_timeout_ns, status,
+                static_cast<cudaStream_t>(stream), cos, sin};
+  return tk::launch_attn_fwd(a);
+}
+
+int tk_rope_rotate(const void* x, void* out, const float* cos, const float* sin, int64_t batch, int64_t heads,
+                   int64_t seq, int64_t head_dim, int dtype, int transpose, void* stream) {
+  if (x == nullptr || out == nullptr || cos == nullptr || sin == nullptr) return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
+  if (!aligned16(x) || !aligned16(out) || !aligned16(cos) || !aligned16(sin)) return tk::kErrMisaligned;
+  tk::RopeRotateArgs a{x, out, cos, sin, batch * heads * seq, seq, head_dim, dtype == TK_DTYPE_BF16,
+                       transpose != 0, static_cast<cudaStream_t>(stream)};
+  return tk::launch_rope_rotate(a);
+}
+
+int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float* cos, const float* sin, int64_t batch,
+                            int64_t heads, int64_t seq, int64_t head_dim, int dtype, void* stream) {
+  if (dq_accum == nullptr || dq == nullptr || cos == nullptr || sin == nullptr) return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
+  if (!aligned16(dq_accum) || !aligned16(dq) || !aligned16(cos) || !aligned16(sin)) return tk::kErrMisaligned;
+  tk::DqConvertRopeArgs a{dq_accum, dq, cos, sin, batch * heads * seq, seq, head_dim, dtype == TK_DTYPE_BF16,
+                          static_cast<cudaStream_t>(stream)};
+  return tk::launch_dq_convert_rope(a);
+}
+
 int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream) {
   if (dq_accum == nullptr || dq == nullptr || n <= 0 || n % 8 != 0) return tk::kErrInvalidArgument;
   if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;

@@ -34,6 +34,7 @@
 // tile.  S_X(j+1) is issued after PV_X(j), so once a softmax warpgroup sees
 // S_X(j+1) complete it may rescale O_X without a separate barrier.
 #include "attn_launch.h"
+#include "rope_sm100.cuh"
 #include "sm100_primitives.cuh"
 
 namespace tk {
@@ -48,8 +49,9 @@ struct FwdCfg {
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   // q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S],
-  // s_full[2], p_ready[2], o_final[2]
-  static constexpr int kNumBars = 2 + 4 * kStages + 6;
+  // s_full[2], p_ready[2], o_final[2], q_rot, k_rot[S] (the last two only
+  // used with RoPE)
+  static constexpr int kNumBars = 3 + 5 * kStages + 6;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -210,11 +212,15 @@ __device__ __forceinline__ void fwd_unit_item(int u, int sub, int BH, int n_ctil
   }
 }
 
-template <int D, bool kBf16>
+// kRope: rotate-half RoPE (tables rope_cos / rope_sin, (S, D/2) fp32) is
+// applied to every Q and K tile in shared memory after its TMA load and
+// before any MMA reads it, by WG0's otherwise idle warps 2 and 3.
+template <int D, bool kBf16, bool kRope>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                    uint16_t* __restrict__ out, float* __restrict__ lse,
+                    uint16_t* __restrict__ out, float* __restrict__ lse, const float* __restrict__ rope_cos,
+                    const float* __restrict__ rope_sin,
                     int S, int BH, int n_ctiles, int causal, int mode, int n_units, int d_real, float scale_log2,
                     unsigned long long timeout_ns, int* status) {
   using C = FwdCfg<D>;
@@ -241,6 +247,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* s_full = v_empty + C::kStages;  // [2]
   uint64_t* p_ready = s_full + 2;           // [2]
   uint64_t* o_final = p_ready + 2;          // [2]
+  uint64_t* q_rot = o_final + 2;
+  uint64_t* k_rot = q_rot + 1;              // [kStages]
+  // With RoPE the MMA warp consumes the rotated tiles.
+  uint64_t* q_mma = kRope ? q_rot : q_full;
+  uint64_t* k_mma = kRope ? k_rot : k_full;
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
@@ -257,6 +268,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&p_ready[i], 4);
       mbar_init(&o_final[i], 1);
     }
+    mbar_init(q_rot, 2);  // the two rotating warps
+    for (int i = 0; i < C::kStages; ++i) mbar_init(&k_rot[i], 2);
     ctl->abort = 0;
     fence_mbarrier_init();
   }
@@ -311,6 +324,36 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
               tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
+          }
+        }
+      }
+    } else if (kRope && (warp == 2 || warp == 3)) {
+      // ---------------- RoPE: rotate each landed Q and K tile in place ----------------
+      const int rtid = (warp - 2) * 32 + lane;
+      uint32_t g = 0;
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
+        const int n_sub = fwd_unit_items(u, n_ctiles, mode);
+        for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
+          int bh, ct;
+          fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
+          const int m0 = ct * 2 * kTileRows;
+          const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
+          if (!(ok = warp_wait(q_full, it & 1, ctl, timeout_ns, status, 14))) break;
+#pragma unroll 1
+          for (int x = 0; x < 2; ++x)
+            rope_rotate_tile<D, kBf16>(sQ + x * C::kTileBytes, m0 + x * kTileRows, S, rope_cos, rope_sin, rtid, 64);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(q_rot);
+          for (int j = 0; j < n_kv_b; ++j, ++g) {
+            const int st = g % C::kStages;
+            if (!(ok = warp_wait(&k_full[st], (g / C::kStages) & 1, ctl, timeout_ns, status, 15))) break;
+            rope_rotate_tile<D, kBf16>(sK + st * C::kTileBytes, j * kTileRows, S, rope_cos, rope_sin, rtid, 64);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&k_rot[st]);
           }
         }
       }
@@ -369,10 +412,10 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
           // S_x(0) overwrites the previous item's P_x, whose P.V was issued
           // earlier on this thread: the tensor pipe keeps that order.
-          if (!(ok = warp_wait(q_full, it & 1, ctl, timeout_ns, status, 3))) break;
+          if (!(ok = warp_wait(q_mma, it & 1, ctl, timeout_ns, status, 3))) break;
           {
             const int st0 = g % C::kStages;
-            if (!(ok = warp_wait(&k_full[st0], (g / C::kStages) & 1, ctl, timeout_ns, status, 4))) break;
+            if (!(ok = warp_wait(&k_mma[st0], (g / C::kStages) & 1, ctl, timeout_ns, status, 4))) break;
             tc_fence_after();
             issue_s(0, st0);
             issue_s(1, st0);
@@ -397,7 +440,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               tc_fence_after();
               issue_pv(0, st, j > 0);
               if (j1 < n_kv_a) {
-                if (!(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
+                if (!(ok = warp_wait(&k_mma[st1], ph1, ctl, timeout_ns, status, 7))) break;
                 k_ready = true;
                 issue_s(0, st1);
               } else {
@@ -411,7 +454,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             issue_pv(1, st, j > 0);
             commit(&v_empty[st]);
             if (j1 < n_kv_b) {
-              if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
+              if (!k_ready && !(ok = warp_wait(&k_mma[st1], ph1, ctl, timeout_ns, status, 10))) break;
               issue_s(1, st1);
               commit(&k_empty[st1]);
               if (j1 == n_kv_b - 1) commit(q_empty);  // the item's last S product
@@ -564,11 +607,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   }
 }
 
-template <int D, bool kBf16>
+template <int D, bool kBf16, bool kRope>
 int launch_fwd_t(const FwdArgs& a) {
   using C = FwdCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "forward shared memory exceeds the sm_100 limit");
-  auto kern = attn_fwd_kernel<D, kBf16>;
+  auto kern = attn_fwd_kernel<D, kBf16, kRope>;
   static bool attr_set[64] = {};
   static int sm_count[64] = {};
   int dev = 0;
@@ -611,7 +654,8 @@ int launch_fwd_t(const FwdArgs& a) {
   }
   if (n_units > INT32_MAX || grid > INT32_MAX) return kErrTooLarge;
   kern<<<static_cast<unsigned>(grid), kFwdThreads, C::kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, static_cast<uint16_t*>(a.o), a.lse, static_cast<int>(a.S),
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, static_cast<uint16_t*>(a.o), a.lse, a.rope_cos, a.rope_sin,
+      static_cast<int>(a.S),
       static_cast<int>(a.BH), n_ctiles, a.causal, mode, static_cast<int>(n_units), static_cast<int>(a.D),
       a.scale_log2, a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
@@ -622,8 +666,15 @@ int launch_fwd_t(const FwdArgs& a) {
 int launch_attn_fwd(const FwdArgs& a) {
   // head_dim <= 64 runs the 64-column kernel, 64 < head_dim <= 128 the
   // 128-column one; the tensor maps carry the true width.
-  if (a.D <= 64) return a.bf16 ? launch_fwd_t<64, true>(a) : launch_fwd_t<64, false>(a);
-  if (a.D <= 128) return a.bf16 ? launch_fwd_t<128, true>(a) : launch_fwd_t<128, false>(a);
+  if (a.rope_cos != nullptr || a.rope_sin != nullptr) {
+    // RoPE pairs column c with c + D/2 of full tiles: head_dim 64 or 128.
+    if (a.rope_cos == nullptr || a.rope_sin == nullptr) return kErrInvalidArgument;
+    if (a.D == 64) return a.bf16 ? launch_fwd_t<64, true, true>(a) : launch_fwd_t<64, false, true>(a);
+    if (a.D == 128) return a.bf16 ? launch_fwd_t<128, true, true>(a) : launch_fwd_t<128, false, true>(a);
+    return kErrUnsupported;
+  }
+  if (a.D <= 64) return a.bf16 ? launch_fwd_t<64, true, false>(a) : launch_fwd_t<64, false, false>(a);
+  if (a.D <= 128) return a.bf16 ? launch_fwd_t<128, true, false>(a) : launch_fwd_t<128, false, false>(a);
   return kErrUnsupported;
 }
 

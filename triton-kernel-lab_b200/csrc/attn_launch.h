@@ -22,6 +22,11 @@ struct FwdArgs {
   unsigned long long timeout_ns;
   int* status;
   cudaStream_t stream;
+  // Rotate-half RoPE tables (S, D/2) fp32 applied to Q and K inside the
+  // kernel; both nullptr for plain attention.  Last, so positional
+  // initialisers of the fields above stay valid.
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
 };
 
 struct BwdPreArgs {
@@ -81,7 +86,32 @@ struct DqConvertArgs {
   cudaStream_t stream;
 };
 
+struct RopeRotateArgs {
+  const void* x;
+  void* out;  // may alias x
+  const float* cos;
+  const float* sin;
+  int64_t rows;  // batch * heads * S
+  int64_t S, D;
+  bool bf16;
+  bool transpose;
+  cudaStream_t stream;
+};
+
+struct DqConvertRopeArgs {
+  const float* dq_accum;
+  void* dq;
+  const float* cos;
+  const float* sin;
+  int64_t rows;  // batch * heads * S
+  int64_t S, D;
+  bool bf16;
+  cudaStream_t stream;
+};
+
 int launch_attn_fwd(const FwdArgs& a);
+int launch_rope_rotate(const RopeRotateArgs& a);
+int launch_dq_convert_rope(const DqConvertRopeArgs& a);
 int launch_attn_bwd_pre(const BwdPreArgs& a);
 int launch_attn_bwd(const BwdArgs& a);
 // The fused backward with its dQ path compiled out (dK and dV only; a.tm_dq
