@@ -551,6 +551,80 @@ def run_sweep(args: argparse.Namespace) -> None:
         torch.distributed.destroy_process_group()
 
 
+def run_rope(args: argparse.Namespace) -> None:
+    """Fused rotate-half RoPE attention at the configured shape (1 GPU).
+
+    Times, with CUDA events after an L2 flush: the plain forward, the fused
+    RoPE forward (K rotated once into a workspace, Q rotated in shared memory
+    inside the kernel), the same result unfused (Q and K rotated in device
+    memory by the elementwise kernel, then the plain forward) and the RoPE
+    backward (rotate Q and K, delta + clear, fused backward, dQ conversion
+    with the transpose rotation, dK rotated back).  Prints one JSON line per measurement (not the
+    benchmark's headline line)."""
+    from tklab import _native
+    from tklab.kernels.flash_attention import _NATIVE_DTYPE
+    from tklab.kernels.rope_attention import _launch_backward_rope, rope_tables, rotate
+
+    b, h, s, d, dtype, causal, std = CONFIGS[args.config]
+    bh = args.bh if args.bh is not None else b * h
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    shape = (1, bh, s, d)
+    q, k, v, do = _make_inputs(shape, dtype, std, seed=args.seed, device=device)
+    cos, sin = rope_tables(s, d, device=device)
+    o = torch.empty_like(q)
+    lse = torch.empty((1, bh, s), dtype=torch.float32, device=device)
+    q_r, k_r = torch.empty_like(q), torch.empty_like(k)
+    lib = _native.load()
+    nd = _NATIVE_DTYPE[dtype]
+    scale = 1.0 / math.sqrt(d)
+    sp = int(torch.cuda.current_stream(device).cuda_stream)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def plain() -> None:
+        _native.check(lib.tk_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                      1, bh, s, d, nd, int(causal), scale, sp), "fwd")
+
+    def fused() -> None:
+        _native.check(lib.tk_attn_fwd_rope(q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                           k_r.data_ptr(), o.data_ptr(), lse.data_ptr(), 1, bh, s, d, nd,
+                                           int(causal), scale, sp),
+                      "fwd_rope")
+
+    def unfused() -> None:
+        rotate(q, cos, sin, out=q_r)
+        rotate(k, cos, sin, out=k_r)
+        _native.check(lib.tk_attn_fwd(q_r.data_ptr(), k_r.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                      1, bh, s, d, nd, int(causal), scale, sp), "fwd")
+
+    def backward() -> None:
+        _launch_backward_rope(q, k, v, o, lse, do, cos, sin, causal=causal)
+
+    results = {}
+    for name, fn in (("fwd_plain", plain), ("fwd_rope_fused", fused), ("fwd_rope_unfused", unfused),
+                     ("bwd_rope", backward)):
+        for _ in range(args.warmup):
+            fn()
+        samples = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(device)
+            samples.append(e0.elapsed_time(e1))
+        results[name] = statistics.median(samples)
+    ff, bf = fwd_flops(1, bh, s, d, causal), bwd_flops(1, bh, s, d, causal)
+    for name, ms in results.items():
+        flops = bf if name.startswith("bwd") else ff
+        print(json.dumps({
+            "rope": name, "config": args.config, "bh": bh, "S": s, "D": d, "causal": causal,
+            "dtype": str(dtype).replace("torch.", ""), "ms": round(ms, 4), "tflops": round(flops / ms / 1e9, 1),
+            "vs_fwd_plain": round(ms / results["fwd_plain"], 3) if name.startswith("fwd") else None,
+            "l2": "flushed before every timed call"}), flush=True)
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -569,11 +643,15 @@ def main() -> None:
                         help="ncu dram bytes per launch of the dominant kernel, if captured")
     parser.add_argument("--sweep", action="store_true",
                         help="C5 sweep (fwd and bwd per dtype/causal/D/S), one JSON line per configuration")
+    parser.add_argument("--rope", action="store_true",
+                        help="fused RoPE attention vs plain and unfused, one JSON line per measurement (1 GPU)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
     if args.sweep:
         run_sweep(args)
+    elif args.rope:
+        run_rope(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -140,10 +140,12 @@ TK_API int tk_attn_bwd_deterministic(const void* q, const void* k, const void* v
  * :27-160 fix the arithmetic; this is the step before attention).  Tables
  * cos and sin are (seq, head_dim/2) fp32, indexed by the position only and
  * shared by every batch and head; head_dim must be 64 or 128.
- *   tk_attn_fwd_rope        o = attention(R q, R k, v): the forward kernel
- *                           rotates each Q and K tile in shared memory after
- *                           its load (rotated values rounded to dtype, as the
- *                           reference's separate rope output is); lse as in
+ *   tk_attn_fwd_rope        o = attention(R q, R k, v): K is rotated once
+ *                           into the caller's k_rot workspace (same shape as
+ *                           k; it holds R k on return), and the forward kernel
+ *                           rotates each Q tile in shared memory after its
+ *                           load; rotated values are rounded to dtype, as the
+ *                           reference's separate rope output is; lse as in
  *                           tk_attn_fwd
  *   tk_rope_rotate          out = R x (transpose: R^T x) for a contiguous
  *                           (batch, heads, seq, head_dim) tensor; out may be x.
@@ -153,8 +155,8 @@ TK_API int tk_attn_bwd_deterministic(const void* q, const void* k, const void* v
  *                           tk_attn_dq_convert), and tk_rope_rotate with
  *                           transpose on dk. */
 TK_API int tk_attn_fwd_rope(const void* q, const void* k, const void* v, const float* cos, const float* sin,
-                            void* o, float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
-                            int dtype, int causal, float scale, void* stream);
+                            void* k_rot, void* o, float* lse, int64_t batch, int64_t heads, int64_t seq,
+                            int64_t head_dim, int dtype, int causal, float scale, void* stream);
 TK_API int tk_rope_rotate(const void* x, void* out, const float* cos, const float* sin, int64_t batch,
                           int64_t heads, int64_t seq, int64_t head_dim, int dtype, int transpose, void* stream);
 TK_API int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float* cos, const float* sin,

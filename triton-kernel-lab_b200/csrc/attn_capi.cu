@@ -177,23 +177,30 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   return tk::launch_attn_bwd(a);
 }
 
-int tk_attn_fwd_rope(const void* q, const void* k, const void* v, const float* cos, const float* sin, void* o,
-                     float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
+int tk_attn_fwd_rope(const void* q, const void* k, const void* v, const float* cos, const float* sin, void* k_rot,
+                     void* o, float* lse, int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
                      int causal, float scale, void* stream) {
-  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || cos == nullptr || sin == nullptr)
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || cos == nullptr || sin == nullptr ||
+      k_rot == nullptr)
     return tk::kErrInvalidArgument;
   if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
   if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
   if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
-  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(cos) || !aligned16(sin))
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(cos) || !aligned16(sin) ||
+      !aligned16(k_rot))
     return tk::kErrMisaligned;
   if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u)) return tk::kErrMisaligned;
   int* status = nullptr;
   if (int rc = status_ptr(&status)) return rc;
   const int64_t bh = batch * heads;
+  // K once, into the caller's workspace (every CTA streams every K tile);
+  // Q inside the kernel, once per query tile.
+  tk::RopeRotateArgs rk{k, k_rot, cos, sin, bh * seq, seq, head_dim, dtype == TK_DTYPE_BF16, false,
+                        static_cast<cudaStream_t>(stream)};
+  if (int rc = tk::launch_rope_rotate(rk)) return rc;
   CUtensorMap mq, mk, mv, mo;
   if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
-  if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+  if (int rc = make_map(&mk, k_rot, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mo, o, bh, seq, head_dim, dtype)) return rc;
   tk::FwdArgs a{&mq, &mk, &mv, &mo, o, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16,

@@ -49,9 +49,9 @@ struct FwdCfg {
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   // q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S],
-  // s_full[2], p_ready[2], o_final[2], q_rot, k_rot[S] (the last two only
-  // used with RoPE)
-  static constexpr int kNumBars = 3 + 5 * kStages + 6;
+  // s_full[2], p_ready[2], o_final[2], q_rot[2] (the last only used with
+  // RoPE)
+  static constexpr int kNumBars = 2 + 4 * kStages + 8;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -213,8 +213,12 @@ __device__ __forceinline__ void fwd_unit_item(int u, int sub, int BH, int n_ctil
 }
 
 // kRope: rotate-half RoPE (tables rope_cos / rope_sin, (S, D/2) fp32) is
-// applied to every Q and K tile in shared memory after its TMA load and
-// before any MMA reads it, by WG0's otherwise idle warps 2 and 3.
+// applied to each item's Q tiles in shared memory after their TMA load and
+// before the S products read them, by the softmax warpgroups (thread r
+// rotates row r of its own tile) at the start of the item, where they would
+// otherwise wait for S(0).  K arrives rotated (the caller rotates it once:
+// every CTA streams every K tile, so rotating K here would repeat the work
+// once per query tile).
 template <int D, bool kBf16, bool kRope>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -247,11 +251,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   uint64_t* s_full = v_empty + C::kStages;  // [2]
   uint64_t* p_ready = s_full + 2;           // [2]
   uint64_t* o_final = p_ready + 2;          // [2]
-  uint64_t* q_rot = o_final + 2;
-  uint64_t* k_rot = q_rot + 1;              // [kStages]
-  // With RoPE the MMA warp consumes the rotated tiles.
-  uint64_t* q_mma = kRope ? q_rot : q_full;
-  uint64_t* k_mma = kRope ? k_rot : k_full;
+  uint64_t* q_rot = o_final + 2;           // [2]: Q_x rotated (RoPE)
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
@@ -268,8 +268,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&p_ready[i], 4);
       mbar_init(&o_final[i], 1);
     }
-    mbar_init(q_rot, 2);  // the two rotating warps
-    for (int i = 0; i < C::kStages; ++i) mbar_init(&k_rot[i], 2);
+    mbar_init(&q_rot[0], 4);  // the four warps of softmax warpgroup x
+    mbar_init(&q_rot[1], 4);
     ctl->abort = 0;
     fence_mbarrier_init();
   }
@@ -324,36 +324,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
               tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
-          }
-        }
-      }
-    } else if (kRope && (warp == 2 || warp == 3)) {
-      // ---------------- RoPE: rotate each landed Q and K tile in place ----------------
-      const int rtid = (warp - 2) * 32 + lane;
-      uint32_t g = 0;
-      int it = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const int n_sub = fwd_unit_items(u, n_ctiles, mode);
-        for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
-          int bh, ct;
-          fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-          const int m0 = ct * 2 * kTileRows;
-          const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
-          if (!(ok = warp_wait(q_full, it & 1, ctl, timeout_ns, status, 14))) break;
-#pragma unroll 1
-          for (int x = 0; x < 2; ++x)
-            rope_rotate_tile<D, kBf16>(sQ + x * C::kTileBytes, m0 + x * kTileRows, S, rope_cos, rope_sin, rtid, 64);
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(q_rot);
-          for (int j = 0; j < n_kv_b; ++j, ++g) {
-            const int st = g % C::kStages;
-            if (!(ok = warp_wait(&k_full[st], (g / C::kStages) & 1, ctl, timeout_ns, status, 15))) break;
-            rope_rotate_tile<D, kBf16>(sK + st * C::kTileBytes, j * kTileRows, S, rope_cos, rope_sin, rtid, 64);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&k_rot[st]);
           }
         }
       }
@@ -412,12 +382,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
           // S_x(0) overwrites the previous item's P_x, whose P.V was issued
           // earlier on this thread: the tensor pipe keeps that order.
-          if (!(ok = warp_wait(q_mma, it & 1, ctl, timeout_ns, status, 3))) break;
+          if (!(ok = warp_wait(kRope ? &q_rot[0] : q_full, it & 1, ctl, timeout_ns, status, 3))) break;
           {
             const int st0 = g % C::kStages;
-            if (!(ok = warp_wait(&k_mma[st0], (g / C::kStages) & 1, ctl, timeout_ns, status, 4))) break;
+            if (!(ok = warp_wait(&k_full[st0], (g / C::kStages) & 1, ctl, timeout_ns, status, 4))) break;
             tc_fence_after();
             issue_s(0, st0);
+            if (kRope) {
+              if (!(ok = warp_wait(&q_rot[1], it & 1, ctl, timeout_ns, status, 14))) break;
+              tc_fence_after();
+            }
             issue_s(1, st0);
             commit(&k_empty[st0]);
             if (n_kv_b == 1) commit(q_empty);
@@ -440,7 +414,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
               tc_fence_after();
               issue_pv(0, st, j > 0);
               if (j1 < n_kv_a) {
-                if (!(ok = warp_wait(&k_mma[st1], ph1, ctl, timeout_ns, status, 7))) break;
+                if (!(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 7))) break;
                 k_ready = true;
                 issue_s(0, st1);
               } else {
@@ -454,7 +428,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             issue_pv(1, st, j > 0);
             commit(&v_empty[st]);
             if (j1 < n_kv_b) {
-              if (!k_ready && !(ok = warp_wait(&k_mma[st1], ph1, ctl, timeout_ns, status, 10))) break;
+              if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
               issue_s(1, st1);
               commit(&k_empty[st1]);
               if (j1 == n_kv_b - 1) commit(q_empty);  // the item's last S product
@@ -488,8 +462,20 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const int m0 = ct * 2 * kTileRows;
         const int row_g = m0 + x * kTileRows + r;
         const int n_kv_x = causal ? min(2 * ct + 1 + x, n_ntiles) : n_ntiles;
+        if constexpr (kRope) {
+          // Rotate this thread's row of Q_x once the item's Q has landed.
+          // (No early exit: after a failed wait the warps still reach the
+          // epilogue's warpgroup barrier.)
+          if (ok) ok = warp_wait(q_full, it & 1, ctl, timeout_ns, status, 15);
+          if (ok) {
+            rope_rotate_row<D, kBf16>(sQ + x * C::kTileBytes, r, row_g, S, rope_cos, rope_sin);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&q_rot[x]);
+          }
+        }
         float m_run = -INFINITY, l_run = 0.0f;
-        for (int j = 0; j < n_kv_x; ++j, ++cs) {
+        for (int j = 0; ok && j < n_kv_x; ++j, ++cs) {
           if (!(ok = warp_wait(&s_full[x], cs & 1, ctl, timeout_ns, status, 11))) break;
           tc_fence_after();
           const int n0 = j * kTileRows;

@@ -59,32 +59,29 @@ __device__ __forceinline__ void rope_rotate8(float (&a)[8], float (&b)[8], const
   }
 }
 
-// Rotate, in shared memory, the rows of one 128-row tile stored in the
-// 128-byte-swizzled column-block layout (D = 64 or 128 columns).  Tile row r
-// holds position pos0 + r; rows at or past `S` (zero-filled by the tile load)
-// are left alone.  Threads tid = 0..nthreads-1 share the work: a work unit is
-// one row's pair of 16-byte chunks (columns c..c+7 and c+h..c+h+7), which sit
-// at the same offset of the two column blocks for D = 128 and in chunks k,
-// k+4 of the one block for D = 64.
+// Rotate, in shared memory, row r of a 128-row tile stored in the
+// 128-byte-swizzled column-block layout (D = 64 or 128 columns), whose
+// position is `pos` (rows at or past `S`, zero-filled by the tile load, are
+// left alone).  Column c pairs with c + D/2: for D = 128 the two 16-byte
+// chunks sit at the same offset of the two column blocks, for D = 64 in
+// chunks k and k + 4 of the one block.  One thread rotates its whole row
+// (the calling warpgroup has a thread per row and registers to keep every
+// load of the row in flight).
 template <int D, bool kBf16>
-__device__ __forceinline__ void rope_rotate_tile(uint8_t* tile, int pos0, int S, const float* __restrict__ cos_t,
-                                                 const float* __restrict__ sin_t, int tid, int nthreads) {
+__device__ __forceinline__ void rope_rotate_row(uint8_t* tile, int r, int pos, int S, const float* __restrict__ cos_t,
+                                                const float* __restrict__ sin_t) {
   constexpr int kHalf = D / 2;
-  constexpr int kChunkPairs = kHalf / 8;  // per row
-  for (int u = tid; u < kTileRows * kChunkPairs; u += nthreads) {
-    const int r = u / kChunkPairs;
-    const int k = u % kChunkPairs;
-    const int pos = pos0 + r;
-    if (pos >= S) continue;
-    const uint32_t off_a = swz_offset(r, 8 * k, kTileRows);
-    const uint32_t off_b = swz_offset(r, 8 * k + kHalf, kTileRows);
-    uint4* pa = reinterpret_cast<uint4*>(tile + off_a);
-    uint4* pb = reinterpret_cast<uint4*>(tile + off_b);
+  if (pos >= S) return;
+  const float* cs = cos_t + static_cast<size_t>(pos) * kHalf;
+  const float* sn = sin_t + static_cast<size_t>(pos) * kHalf;
+#pragma unroll
+  for (int k = 0; k < kHalf / 8; ++k) {
+    uint4* pa = reinterpret_cast<uint4*>(tile + swz_offset(r, 8 * k, kTileRows));
+    uint4* pb = reinterpret_cast<uint4*>(tile + swz_offset(r, 8 * k + kHalf, kTileRows));
     float a[8], b[8];
     unpack8<kBf16>(*pa, a);
     unpack8<kBf16>(*pb, b);
-    const size_t t = static_cast<size_t>(pos) * kHalf + 8 * k;
-    rope_rotate8<false>(a, b, cos_t + t, sin_t + t);
+    rope_rotate8<false>(a, b, cs + 8 * k, sn + 8 * k);
     *pa = pack8<kBf16>(a);
     *pb = pack8<kBf16>(b);
   }

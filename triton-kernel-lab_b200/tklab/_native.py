@@ -70,7 +70,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "tk_attn_fwd_rope": (
         ctypes.c_int,
-        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp],
+        [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp],
     ),
     "tk_rope_rotate": (
         ctypes.c_int,

@@ -1,4 +1,4 @@
-"""Flash attention with rotate-half RoPE fused into the Q/K tile loads (B200).
+"""Flash attention with rotate-half RoPE fused into the Q tile loads (B200).
 
 ``attention_rope(q, k, v, cos, sin, causal=...)`` computes
 ``attention(rope(q), rope(k), v)`` where ``rope`` is the reference's
@@ -7,8 +7,11 @@ public ``rope`` at ``:310-316``): for position p and half width h,
 ``out[:h] = x[:h] cos[p] - x[h:] sin[p]``, ``out[h:] = x[h:] cos[p] + x[:h]
 sin[p]``, in fp32, rounded to the input dtype.  In the reference, RoPE is a
 separate 2-D op run before attention; here the forward kernel rotates each
-Q and K tile in shared memory right after its TMA load, so the rotated
-tensors never exist in device memory.
+Q tile in shared memory right after its TMA load (the rotated Q never
+exists in device memory), and K is rotated once into a workspace by an
+elementwise pass: every CTA streams every K tile, so rotating K inside the
+kernel would repeat the rotation once per query tile (measured 3x slower
+than this split).
 
 Tables ``cos`` and ``sin`` are ``(seq_len, head_dim // 2)`` (any float
 dtype; converted to contiguous fp32), indexed by the position only and
@@ -16,15 +19,17 @@ shared by every batch and head.  head_dim must be 64 or 128.  They are
 treated as constants: no gradient flows to them (the reference's ``rope``
 returns table gradients; its attention has no RoPE).
 
-Backward: the rotated Q and K are materialised once (``tk_rope_rotate``),
-the fused backward runs on them, and the gradients are rotated back with
-the transpose rotation (``tk_attn_dq_convert_rope`` for dQ, in place on dK),
-exactly the chain rule of ``attention(R q, R k, v)``.
+Backward: the rotated Q is materialised (``tk_rope_rotate``; the forward's
+rotated K is reused), the fused backward runs on them, and the gradients
+are rotated back with the transpose rotation (``tk_attn_dq_convert_rope``
+for dQ, in place on dK), exactly the chain rule of ``attention(R q, R k,
+v)``.
 """
 
 from __future__ import annotations
 
 import math
+from functools import partial
 from typing import Any, cast
 
 import torch
@@ -44,7 +49,7 @@ from tklab.kernels.flash_attention import (
     _stream,
     _validate,
 )
-from tklab.registry import KernelSpec, LaunchFn, TensorArgs, TensorFn, register
+from tklab.registry import BenchmarkCall, BenchmarkCallFactory, KernelSpec, LaunchFn, TensorArgs, TensorFn, register
 
 ROPE_HEAD_DIMS = (64, 128)
 _ROPE_HEAD_DIM = 64  # registered benchmark problem: the reference attention shape
@@ -82,17 +87,20 @@ def _launch_forward_rope(
     sin32: torch.Tensor,
     output: torch.Tensor,
     softmax_lse: torch.Tensor | None,
+    k_rot: torch.Tensor,
     *,
     causal: bool,
 ) -> None:
-    """Launch the fused RoPE forward into preallocated buffers (LSE when given)."""
+    """Launch the RoPE forward into preallocated buffers (LSE when given); ``k_rot`` receives R k."""
     batch, heads, n_ctx, head_dim = q.shape
     if output.shape != q.shape or output.dtype != q.dtype or not output.is_contiguous():
         raise ValueError("attention output metadata must match Q")
+    if k_rot.shape != k.shape or k_rot.dtype != k.dtype or not k_rot.is_contiguous():
+        raise ValueError("rotated-K workspace metadata must match K")
     lib = _native.load()
     with torch.cuda.device(q.device):
         status = lib.tk_attn_fwd_rope(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos32.data_ptr(), sin32.data_ptr(),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), cos32.data_ptr(), sin32.data_ptr(), k_rot.data_ptr(),
             output.data_ptr(), None if softmax_lse is None else softmax_lse.data_ptr(),
             batch, heads, n_ctx, head_dim, _NATIVE_DTYPE[q.dtype], int(bool(causal)),
             1.0 / math.sqrt(head_dim), _stream(q),
@@ -129,14 +137,18 @@ def _launch_backward_rope(
     sin32: torch.Tensor,
     *,
     causal: bool,
+    k_rot: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Gradients of ``attention(R q, R k, v)``: the fused backward on (R q, R k), then R^T."""
+    """Gradients of ``attention(R q, R k, v)``: the fused backward on (R q, R k), then R^T.
+
+    ``k_rot`` (R k, kept from the forward) saves rotating K again."""
     if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
         raise ValueError("attention upstream gradient metadata must match Q")
     do = do.contiguous()
     batch, heads, n_ctx, head_dim = q.shape
     q_rot = rotate(q, cos32, sin32)
-    k_rot = rotate(k, cos32, sin32)
+    if k_rot is None:
+        k_rot = rotate(k, cos32, sin32)
     delta = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
     dq_accum = torch.empty((batch, heads, n_ctx, head_dim), dtype=torch.float32, device=q.device)
     dq = torch.empty_like(q)
@@ -185,8 +197,9 @@ class _RopeAttentionFunction(torch.autograd.Function):
         output = torch.empty_like(q)
         batch, heads, n_ctx, _ = q.shape
         softmax_lse = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
-        _launch_forward_rope(q, k, v, cos32, sin32, output, softmax_lse, causal=causal)
-        ctx.save_for_backward(q, k, v, output, softmax_lse, cos32, sin32)
+        k_rot = torch.empty_like(k)
+        _launch_forward_rope(q, k, v, cos32, sin32, output, softmax_lse, k_rot, causal=causal)
+        ctx.save_for_backward(q, k, v, output, softmax_lse, cos32, sin32, k_rot)
         ctx.causal = causal
         return output
 
@@ -194,8 +207,10 @@ class _RopeAttentionFunction(torch.autograd.Function):
     @once_differentiable
     def backward(ctx: Any, do: torch.Tensor) -> tuple[Any, ...]:
         """Q, K and V gradients; the tables are constants."""
-        q, k, v, output, softmax_lse, cos32, sin32 = ctx.saved_tensors
-        dq, dk, dv = _launch_backward_rope(q, k, v, output, softmax_lse, do, cos32, sin32, causal=ctx.causal)
+        q, k, v, output, softmax_lse, cos32, sin32, k_rot = ctx.saved_tensors
+        dq, dk, dv = _launch_backward_rope(
+            q, k, v, output, softmax_lse, do, cos32, sin32, causal=ctx.causal, k_rot=k_rot
+        )
         return dq, dk, dv, None, None, None
 
 
@@ -213,7 +228,7 @@ def attention_rope(
     needs_grad = torch.is_grad_enabled() and any(t.requires_grad for t in (q, k, v))
     if not needs_grad:
         output = torch.empty_like(q)
-        _launch_forward_rope(q, k, v, cos32, sin32, output, None, causal=causal)
+        _launch_forward_rope(q, k, v, cos32, sin32, output, None, torch.empty_like(k), causal=causal)
         return output
     return cast(torch.Tensor, _RopeAttentionFunction.apply(q, k, v, cos, sin, causal))
 
@@ -284,14 +299,26 @@ def _make_output(args: TensorArgs) -> torch.Tensor:
 
 
 def _launch_factory(*, causal: bool) -> LaunchFn:
-    """Allocation-free inference launcher (no LSE) for one masking mode."""
+    """Inference launcher (no LSE) for one masking mode."""
 
     def launch(args: TensorArgs, output: torch.Tensor) -> None:
         q, k, v, cos, sin = args
         cos32, sin32 = _validate_rope(q, k, v, cos, sin)
-        _launch_forward_rope(q, k, v, cos32, sin32, output, None, causal=causal)
+        _launch_forward_rope(q, k, v, cos32, sin32, output, None, torch.empty_like(k), causal=causal)
 
     return launch
+
+
+def _benchmark_call_factory(*, causal: bool) -> BenchmarkCallFactory:
+    """Benchmark call with the tables converted and the K workspace allocated up front."""
+
+    def factory(args: TensorArgs, output: torch.Tensor) -> BenchmarkCall:
+        q, k, v, cos, sin = args
+        cos32, sin32 = _validate_rope(q, k, v, cos, sin)
+        k_rot = torch.empty_like(k)
+        return partial(_launch_forward_rope, q, k, v, cos32, sin32, output, None, k_rot, causal=causal)
+
+    return factory
 
 
 def _assert_rope_attention(output: torch.Tensor, reference: torch.Tensor) -> None:
@@ -303,7 +330,7 @@ _SIZES = (512, 1024, 2048, 4096, 8192)
 ATTENTION_ROPE_NONCAUSAL = register(
     KernelSpec(
         name="attention_rope_noncausal",
-        description="Flash Attention forward (sm_100a) with rotate-half RoPE fused into the Q/K tile loads.",
+        description="Flash Attention forward (sm_100a) with rotate-half RoPE: Q rotated in the tile loads, K once.",
         triton_fn=attention_rope_noncausal,
         launch_fn=_launch_factory(causal=False),
         ref_fn=_reference_factory(causal=False),
@@ -317,6 +344,7 @@ ATTENTION_ROPE_NONCAUSAL = register(
         dtypes=(torch.float16, torch.bfloat16),
         assert_fn=_assert_rope_attention,
         benchmark_metadata=_metadata_factory(causal=False),
+        benchmark_call_factory=_benchmark_call_factory(causal=False),
         compute_mode="attention_fp16_fp32acc",
         supports_interpreter=False,
     )
@@ -325,7 +353,7 @@ ATTENTION_ROPE_NONCAUSAL = register(
 ATTENTION_ROPE_CAUSAL = register(
     KernelSpec(
         name="attention_rope_causal",
-        description="Causal Flash Attention forward (sm_100a) with rotate-half RoPE fused into the Q/K tile loads.",
+        description="Causal Flash Attention forward (sm_100a) with rotate-half RoPE: Q rotated in the tile loads, K once.",
         triton_fn=attention_rope_causal,
         launch_fn=_launch_factory(causal=True),
         ref_fn=_reference_factory(causal=True),
@@ -339,6 +367,7 @@ ATTENTION_ROPE_CAUSAL = register(
         dtypes=(torch.float16, torch.bfloat16),
         assert_fn=_assert_rope_attention,
         benchmark_metadata=_metadata_factory(causal=True),
+        benchmark_call_factory=_benchmark_call_factory(causal=True),
         compute_mode="attention_fp16_fp32acc",
         supports_interpreter=False,
     )
