@@ -625,6 +625,57 @@ def run_rope(args: argparse.Namespace) -> None:
             "l2": "flushed before every timed call"}), flush=True)
 
 
+def run_decode(args: argparse.Namespace) -> None:
+    """GQA decode (``tk_gqa_decode``) at the reference model's numerical point
+    (B=1, Hq=32, Hkv=8, Dh=128, L=4096, fp16) and larger batch / context
+    shapes, 1 GPU.  Each shape is timed with CUDA events in the two cache
+    states the model asks to keep apart: "controlled cache-thrashing" (a
+    256 MiB write evicts L2 before every call) and warm (back-to-back calls).
+    Reported against the model's minimum traffic (unique KV + Q + O bytes)
+    and the measured HBM copy bandwidth; one JSON line per shape."""
+    from tklab.kernels.gqa_decode import decode_model, gqa_decode
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peaks = _peaks()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    shapes = [(1, 32, 8, 128, 4096), (1, 32, 8, 128, 131072), (32, 32, 8, 128, 4096), (64, 32, 8, 128, 8192),
+              (16, 64, 8, 128, 16384)]
+    for batch, hq, hkv, d, seq in shapes:
+        g = torch.Generator(device=device).manual_seed(args.seed)
+        q = torch.randn((batch, hq, d), generator=g, device=device).to(torch.float16)
+        k = torch.randn((batch, hkv, seq, d), generator=g, device=device).to(torch.float16)
+        v = torch.randn((batch, hkv, seq, d), generator=g, device=device).to(torch.float16)
+        model = decode_model(batch, hq, hkv, d, seq)
+        times = {}
+        for state in ("l2_flushed", "warm"):
+            for _ in range(args.warmup):
+                gqa_decode(q, k, v)
+            samples = []
+            for _ in range(args.steps):
+                if state == "l2_flushed":
+                    flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                gqa_decode(q, k, v)
+                e1.record()
+                torch.cuda.synchronize(device)
+                samples.append(e0.elapsed_time(e1))
+            times[state] = statistics.median(samples)
+        ms = times["l2_flushed"]
+        gbs = model.bytes_min / (ms * 1e-3) / 1e9
+        print(json.dumps({
+            "decode": "gqa", "B": batch, "Hq": hq, "Hkv": hkv, "G": hq // hkv, "Dh": d, "L": seq,
+            "dtype": "float16", "ms_l2_flushed": round(ms, 4), "ms_warm": round(times["warm"], 4),
+            "bytes_min": model.bytes_min, "gbs_of_bytes_min": round(gbs, 1),
+            "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 3) if peaks.get("hbm_gbs") else None,
+            "useful_tflops": round(model.flops_useful / (ms * 1e-3) / 1e12, 2),
+            "intensity_min": round(model.intensity_min, 4),
+            "timing": "CUDA events, median; includes the split and combine kernels and the workspace allocation",
+        }), flush=True)
+        del q, k, v
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -643,6 +694,8 @@ def main() -> None:
                         help="ncu dram bytes per launch of the dominant kernel, if captured")
     parser.add_argument("--sweep", action="store_true",
                         help="C5 sweep (fwd and bwd per dtype/causal/D/S), one JSON line per configuration")
+    parser.add_argument("--decode", action="store_true",
+                        help="GQA decode at the reference model's shapes, one JSON line per shape (1 GPU)")
     parser.add_argument("--rope", action="store_true",
                         help="fused RoPE attention vs plain and unfused, one JSON line per measurement (1 GPU)")
     args = parser.parse_args()
@@ -652,6 +705,8 @@ def main() -> None:
         run_sweep(args)
     elif args.rope:
         run_rope(args)
+    elif args.decode:
+        run_decode(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -163,6 +163,25 @@ TK_API int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float*
                                    int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
                                    void* stream);
 
+/* Grouped-query-attention decode: one query token per query head, q_heads =
+ * G * kv_heads (query head h reads KV head h / G), contiguous KV cache.
+ * The reference specifies this workload as a model only
+ * (docs/research/gqa_decode_model.md: "Canonical decode workload",
+ * "Semantic GQA mapping"); it has no kernel.
+ *   q, o     (batch, q_heads, head_dim)         16-bit
+ *   k, v     (batch, kv_heads, seq_kv, head_dim) 16-bit
+ *   kv_lens  (batch) int32 valid keys per batch (clamped to [0, seq_kv]),
+ *            or NULL for all seq_kv; a batch with none gets o = 0, lse = -inf
+ *   lse      (batch, q_heads) fp32 base-2 log-sum-exp (scale included), or NULL
+ *   o = softmax(q . K^T * scale) V over the valid keys.  G in {1, 2, 4, 8,
+ *   16}, head_dim 64 or 128.  Split-KV: chunks of 64 keys per CTA (K and V
+ *   by bulk copy into shared memory) and a combine pass; the partials live
+ *   in `workspace`, at least tk_gqa_decode_workspace_bytes(...) bytes. */
+TK_API size_t tk_gqa_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t seq_kv, int64_t head_dim);
+TK_API int tk_gqa_decode(const void* q, const void* k, const void* v, const int32_t* kv_lens, void* o, float* lse,
+                         void* workspace, size_t workspace_bytes, int64_t batch, int64_t q_heads,
+                         int64_t kv_heads, int64_t seq_kv, int64_t head_dim, int dtype, float scale, void* stream);
+
 /* Bytes of the fp32 dQ accumulator tk_attn_bwd needs (0 on bad sizes). */
 TK_API size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);
 

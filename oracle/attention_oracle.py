@@ -30,6 +30,11 @@ the triton-kernel-lab project):
   reference's two-op pipeline rope → attention with its chain rule, for the
   fused RoPE attention.
 
+* ``gqa_decode_reference`` — grouped-query decode as the reference's model
+  defines it (``docs/research/gqa_decode_model.md``, "Semantic GQA
+  mapping": query head h reads KV head h // G), softmax attention of one
+  query token in fp32 over each batch's valid keys.
+
 Parity is pinned: ``tests/test_oracle_golden.py`` checks all three against
 golden vectors produced by the reference's own Triton kernels (run under the
 Triton CPU interpreter) and its SDPA/manual references, committed under
@@ -320,3 +325,31 @@ def rope_attention_backward(
     dq = rope_rotate(dq_r, cos, sin, transpose=True)
     dk = rope_rotate(dk, cos, sin, transpose=True)
     return dq, dk, dv
+
+
+def gqa_decode_reference(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kv_lens: torch.Tensor | None = None
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o, base-2 lse) of one-token GQA decode in fp32 on the CPU.
+
+    q (B, Hq, D), k/v (B, Hkv, L, D); a batch with no valid key gets o = 0
+    and lse = -inf.
+    """
+    qf, kf, vf = (t.detach().float().cpu() for t in (q, k, v))
+    batch, q_heads, dim = qf.shape
+    kv_heads, seq = kf.shape[1], kf.shape[2]
+    group = q_heads // kv_heads
+    scale = dim ** -0.5
+    out = torch.zeros(batch, q_heads, dim)
+    lse = torch.full((batch, q_heads), -torch.inf)
+    for b in range(batch):
+        n = seq if kv_lens is None else max(0, min(int(kv_lens[b]), seq))
+        if n == 0:
+            continue
+        for h in range(q_heads):
+            kh, vh = kf[b, h // group, :n], vf[b, h // group, :n]
+            scores = (kh @ qf[b, h]) * scale
+            probs = torch.softmax(scores, dim=0)
+            out[b, h] = probs @ vh
+            lse[b, h] = torch.logsumexp(scores, dim=0) / math.log(2.0)
+    return out, lse

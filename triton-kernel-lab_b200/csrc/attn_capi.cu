@@ -231,6 +231,49 @@ int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float* cos, c
   return tk::launch_dq_convert_rope(a);
 }
 
+size_t tk_gqa_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t seq_kv, int64_t head_dim) {
+  if (batch <= 0 || q_heads <= 0 || seq_kv <= 0 || head_dim <= 0) return 0;
+  // Upper bound over every kv_heads and device: one split per 64-key chunk.
+  const int64_t splits = (seq_kv + 63) / 64;
+  const int64_t rows = batch * q_heads * splits;
+  return static_cast<size_t>(rows) * static_cast<size_t>(head_dim + 2) * sizeof(float);
+}
+
+int tk_gqa_decode(const void* q, const void* k, const void* v, const int32_t* kv_lens, void* o, float* lse,
+                  void* workspace, size_t workspace_bytes, int64_t batch, int64_t q_heads, int64_t kv_heads,
+                  int64_t seq_kv, int64_t head_dim, int dtype, float scale, void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || workspace == nullptr)
+    return tk::kErrInvalidArgument;
+  if (batch <= 0 || q_heads <= 0 || kv_heads <= 0 || seq_kv <= 0) return tk::kErrInvalidArgument;
+  if (q_heads % kv_heads != 0) return tk::kErrInvalidArgument;
+  const int64_t group = q_heads / kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8 && group != 16) return tk::kErrUnsupported;
+  if (head_dim != 64 && head_dim != 128) return tk::kErrUnsupported;
+  if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  if (batch > 65535 || kv_heads > 65535 || seq_kv > INT_MAX) return tk::kErrTooLarge;
+  if (batch * kv_heads * seq_kv * head_dim > (int64_t{1} << 40)) return tk::kErrTooLarge;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o) || !aligned16(workspace))
+    return tk::kErrMisaligned;
+  if ((lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u)) ||
+      (kv_lens != nullptr && (reinterpret_cast<uintptr_t>(kv_lens) & 3u)))
+    return tk::kErrMisaligned;
+  if (workspace_bytes < tk_gqa_decode_workspace_bytes(batch, q_heads, seq_kv, head_dim)) return tk::kErrTooLarge;
+  int* status = nullptr;
+  if (int rc = status_ptr(&status)) return rc;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return tk::kErrLaunch;
+  const int splits = tk::gqa_decode_splits(batch, kv_heads, seq_kv, sms);
+  float* part_o = static_cast<float*>(workspace);
+  float* part_ml = part_o + batch * q_heads * splits * head_dim;
+  tk::GqaDecodeArgs a{q, k, v, kv_lens, o, lse, part_o, part_ml, batch, kv_heads, group, seq_kv, head_dim,
+                      splits, dtype == TK_DTYPE_BF16, scale * kLog2e, g_timeout_ns, status,
+                      static_cast<cudaStream_t>(stream)};
+  return tk::launch_gqa_decode(a);
+}
+
 int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream) {
   if (dq_accum == nullptr || dq == nullptr || n <= 0 || n % 8 != 0) return tk::kErrInvalidArgument;
   if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;

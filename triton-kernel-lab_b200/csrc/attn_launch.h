@@ -109,7 +109,28 @@ struct DqConvertRopeArgs {
   cudaStream_t stream;
 };
 
+struct GqaDecodeArgs {
+  const void* q;       // (B, Hkv * G, D)
+  const void* k;       // (B, Hkv, L, D)
+  const void* v;       // (B, Hkv, L, D)
+  const int* kv_lens;  // (B) valid keys per batch, or nullptr (all L)
+  void* o;             // (B, Hkv * G, D)
+  float* lse;          // (B, Hkv * G) base-2 log-sum-exp, or nullptr
+  float* part_o;       // workspace (B, Hkv * G, splits, D)
+  float* part_ml;      // workspace (B, Hkv * G, splits, 2)
+  int64_t B, Hkv, G, L, D;
+  int splits;  // from gqa_decode_splits
+  bool bf16;
+  float scale_log2;
+  unsigned long long timeout_ns;
+  int* status;
+  cudaStream_t stream;
+};
+
 int launch_attn_fwd(const FwdArgs& a);
+int gqa_decode_splits(int64_t B, int64_t Hkv, int64_t L, int sm_count);
+int gqa_decode_keys_per_split(int64_t L, int n_splits);
+int launch_gqa_decode(const GqaDecodeArgs& a);
 int launch_rope_rotate(const RopeRotateArgs& a);
 int launch_dq_convert_rope(const DqConvertRopeArgs& a);
 int launch_attn_bwd_pre(const BwdPreArgs& a);
