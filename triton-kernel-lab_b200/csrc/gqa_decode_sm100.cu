@@ -49,6 +49,31 @@ __device__ __forceinline__ float to_f32(uint16_t h) {
   }
 }
 
+// A lane's N (2 or 4) consecutive 16-bit elements of a shared-memory row, in
+// one 4- or 8-byte load, to fp32.
+template <int N, bool kBf16>
+__device__ __forceinline__ void load_cols(const uint16_t* p, float (&f)[N]) {
+  uint32_t w[N / 2];
+  if constexpr (N == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    w[0] = u.x;
+    w[1] = u.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(p);
+  }
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    if constexpr (kBf16) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    } else {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = x.x;
+      f[2 * i + 1] = x.y;
+    }
+  }
+}
+
 template <int D, int G, bool kBf16>
 __global__ void __launch_bounds__(kDecThreads)
     gqa_decode_split_kernel(const uint16_t* __restrict__ q, const uint16_t* __restrict__ k,
@@ -139,8 +164,7 @@ __global__ void __launch_bounds__(kDecThreads)
         // and dropped.
         const int j = grp * kGroupKeys + kk;
         float kc[kCols];
-#pragma unroll
-        for (int c = 0; c < kCols; ++c) kc[c] = to_f32<kBf16>(sK[j * D + lane * kCols + c]);
+        load_cols<kCols, kBf16>(&sK[j * D + lane * kCols], kc);
 #pragma unroll
         for (int g = 0; g < G; ++g) {
           float acc = 0.0f;
@@ -198,13 +222,16 @@ __global__ void __launch_bounds__(kDecThreads)
     }
     for (int j = warp; j < n_keys; j += 4) {
       float vc[kCols];
-#pragma unroll
-      for (int c = 0; c < kCols; ++c) vc[c] = to_f32<kBf16>(sV[j * D + lane * kCols + c]);
+      load_cols<kCols, kBf16>(&sV[j * D + lane * kCols], vc);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float p = sS[g][j];
+        const uint64_t p2 = f2_pack(p, p);
 #pragma unroll
-        for (int c = 0; c < kCols; ++c) o[g][c] = fmaf(p, vc[c], o[g][c]);
+        for (int c = 0; c < kCols; c += 2) {
+          // Two columns per packed fp32x2 fma.
+          f2_unpack(ffma2(p2, f2_pack(vc[c], vc[c + 1]), f2_pack(o[g][c], o[g][c + 1])), o[g][c], o[g][c + 1]);
+        }
       }
     }
     // sK, sV and sS are reused by the next sub-chunk.
