@@ -53,12 +53,14 @@ int status_ptr(int** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int check_shape(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype) {
+int check_shape(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
+                int64_t max_head_dim = 128) {
   if (batch <= 0 || heads <= 0 || seq <= 0) return tk::kErrInvalidArgument;
-  // Any head_dim up to 128 whose rows are 16-byte multiples: the kernels for
-  // 64 and 128 run it with the tensor maps declaring the true width (loads
-  // zero-fill the missing columns, stores and reductions clip them).
-  if (head_dim < 8 || head_dim > 128 || head_dim % 8 != 0) return tk::kErrUnsupported;
+  // Any head_dim up to the kernel's width whose rows are 16-byte multiples:
+  // the kernels for 64, 128 and 256 run it with the tensor maps declaring the
+  // true width (loads zero-fill the missing columns, stores and reductions
+  // clip them).  Only the forward has a 256-wide kernel.
+  if (head_dim < 8 || head_dim > max_head_dim || head_dim % 8 != 0) return tk::kErrUnsupported;
   if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
   const int64_t bh = batch * heads;
   if (bh > INT_MAX || seq > INT_MAX) return tk::kErrTooLarge;
@@ -67,17 +69,18 @@ int check_shape(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int
   return tk::kOk;
 }
 
-// 3-D map over a contiguous (B*H, S, D) 16-bit tensor: box {64, 128, 1},
-// 128-byte swizzle, zero fill outside the tensor (ragged S tails).
+// 3-D map over a contiguous (B*H, S, D) 16-bit tensor: box {64, box_rows, 1}
+// (128 rows unless a kernel tiles the sequence by 64), 128-byte swizzle, zero
+// fill outside the tensor (ragged S tails).
 int make_map(CUtensorMap* map, const void* base, int64_t bh, int64_t seq, int64_t head_dim,
-             int dtype) {
+             int dtype, uint32_t box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return tk::kErrNoDriver;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq),
                         static_cast<cuuint64_t>(bh)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * 2),
                            static_cast<cuuint64_t>(seq * head_dim * 2)};
-  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t box[3] = {64, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map,
                   dtype == TK_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -116,7 +119,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
                 void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return tk::kErrInvalidArgument;
-  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype, 256)) return rc;
   if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return tk::kErrMisaligned;
   if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u)) return tk::kErrMisaligned;
@@ -124,6 +127,16 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse
   if (int rc = status_ptr(&status)) return rc;
   const int64_t bh = batch * heads;
   CUtensorMap mq, mk, mv, mo;
+  if (head_dim > 128) {
+    // 136..256: one 128-row query tile per CTA against 64-key tiles.
+    if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
+    if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype, 64)) return rc;
+    if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype, 64)) return rc;
+    if (int rc = make_map(&mo, o, bh, seq, head_dim, dtype)) return rc;
+    tk::FwdD256Args a{&mq, &mk, &mv, &mo, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0,
+                      scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
+    return tk::launch_attn_fwd_d256(a);
+  }
   if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;

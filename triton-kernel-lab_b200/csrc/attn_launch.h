@@ -29,6 +29,23 @@ struct FwdArgs {
   const float* rope_sin = nullptr;
 };
 
+// Forward for 128 < head_dim <= 256 (attn_fwd_d256_sm100.cu): Q and O maps
+// with 128-row boxes, K and V maps with 64-row boxes.
+struct FwdD256Args {
+  const CUtensorMap* tm_q;
+  const CUtensorMap* tm_k;
+  const CUtensorMap* tm_v;
+  const CUtensorMap* tm_o;
+  float* lse;
+  int64_t BH, S, D;
+  bool bf16;
+  int causal;
+  float scale_log2;
+  unsigned long long timeout_ns;
+  int* status;
+  cudaStream_t stream;
+};
+
 struct BwdPreArgs {
   const void* o;
   const void* d_o;
@@ -128,6 +145,7 @@ struct GqaDecodeArgs {
 };
 
 int launch_attn_fwd(const FwdArgs& a);
+int launch_attn_fwd_d256(const FwdD256Args& a);
 int gqa_decode_splits(int64_t B, int64_t Hkv, int64_t L, int sm_count);
 int gqa_decode_keys_per_split(int64_t L, int n_splits);
 int launch_gqa_decode(const GqaDecodeArgs& a);

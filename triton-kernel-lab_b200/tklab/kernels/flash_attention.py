@@ -15,7 +15,10 @@ Contract differences from the reference, all widenings:
 * dtypes float16 and bfloat16 (reference: float16 only, ``:281-282``);
 * head_dim any multiple of 8 from 8 to 128 (reference: 64 only,
   ``:283-284``); widths below 64 / 128 run the 64- / 128-column kernels with
-  the tensor maps declaring the true width.
+  the tensor maps declaring the true width;
+* forward only, head_dim 136 to 256 (multiples of 8) on a 256-column kernel
+  (one 128-row query tile per CTA against 64-key tiles); the backward of
+  those widths raises ``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -49,9 +52,12 @@ _HEADS = 16
 _HEAD_DIM = 64
 
 # Head dims the kernels accept: multiples of 8 (16-byte rows for TMA) up to
-# 128.  64 and 128 are the kernels' native widths.
+# 128 for the forward and backward, up to 256 for the forward alone.  64, 128
+# and 256 are the kernels' native widths.
 MAX_HEAD_DIM = 128
 SUPPORTED_HEAD_DIMS = tuple(range(8, MAX_HEAD_DIM + 1, 8))
+MAX_FWD_HEAD_DIM = 256
+SUPPORTED_FWD_HEAD_DIMS = tuple(range(8, MAX_FWD_HEAD_DIM + 1, 8))
 _NATIVE_DTYPE = {torch.float16: _native.TK_DTYPE_F16, torch.bfloat16: _native.TK_DTYPE_BF16}
 
 # Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile
@@ -76,8 +82,12 @@ _CHECK_STATUS = os.environ.get("TKLAB_CHECK_DEVICE_STATUS", "0") == "1"
 _DETERMINISTIC_ENV = os.environ.get("TKLAB_DETERMINISTIC_BWD", "0") == "1"
 
 
-def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
-    """Validate the dense self-attention contract (same order as the reference, ``:267-288``)."""
+def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, max_head_dim: int = MAX_FWD_HEAD_DIM) -> None:
+    """Validate the dense self-attention contract (same order as the reference, ``:267-288``).
+
+    ``max_head_dim`` is the widest head the calling path has a kernel for:
+    256 for the forward, 128 for the backward and the RoPE path.
+    """
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("attention expects Q, K, and V shaped (batch, heads, sequence, dim)")
     if q.shape != k.shape or q.shape != v.shape:
@@ -92,8 +102,12 @@ def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
         raise ValueError("Q, K, and V must have the same dtype")
     if q.dtype not in _NATIVE_DTYPE:
         raise ValueError("attention currently supports float16 and bfloat16 inputs only")
-    if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
-        raise ValueError(f"attention currently requires head_dim to be a multiple of 8 from 8 to {MAX_HEAD_DIM}")
+    if q.shape[-1] % 8 or not 8 <= q.shape[-1] <= MAX_FWD_HEAD_DIM:
+        raise ValueError(f"attention currently requires head_dim to be a multiple of 8 from 8 to {MAX_FWD_HEAD_DIM}")
+    if q.shape[-1] > max_head_dim:
+        raise NotImplementedError(
+            f"attention backward supports head_dim up to {max_head_dim}; head_dim {q.shape[-1]} is forward-only"
+        )
     for name, tensor in (("Q", q), ("K", k), ("V", v)):
         if not tensor.is_contiguous():
             raise ValueError(f"{name} must be contiguous")
@@ -217,7 +231,7 @@ def _launch_backward(
     """
     if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
         raise ValueError("attention upstream gradient metadata must match Q")
-    _validate(q, k, v)
+    _validate(q, k, v, max_head_dim=MAX_HEAD_DIM)
     do = do.contiguous()
     batch, heads, n_ctx, head_dim = q.shape
     if (

@@ -40,6 +40,7 @@ from tklab import _native
 from tklab.harness.addressing import assert_int32_addressable
 from tklab.harness.tolerances import assert_relative_frobenius
 from tklab.kernels.flash_attention import (
+    MAX_HEAD_DIM,
     _BATCH,
     _HEADS,
     _NATIVE_DTYPE,
@@ -69,7 +70,7 @@ def _validate_rope(
             raise ValueError("cos and sin must have shape (seq_len, head_dim // 2)")
     if not (cos.is_floating_point() and sin.is_floating_point()):
         raise ValueError("cos and sin must be floating-point tables")
-    _validate(q, k, v)
+    _validate(q, k, v, max_head_dim=MAX_HEAD_DIM)
     if cos.device != q.device or sin.device != q.device:
         raise ValueError("q, cos, and sin must be on the same device")
     cos32 = cos.detach().to(torch.float32).contiguous()
