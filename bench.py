@@ -676,6 +676,44 @@ def run_decode(args: argparse.Namespace) -> None:
         del q, k, v
 
 
+def run_wide(args: argparse.Namespace) -> None:
+    """Forward for head dims above 128 (the 256-column kernel), 1 GPU, bf16.
+    Each shape: ``--warmup`` calls, then ``--steps`` back-to-back calls timed
+    with CUDA events on the launching stream (Q, K and V are 134-268 MB each,
+    larger than L2).  FLOPs are the reference's forward model, 4·D per
+    attended pair; one JSON line per shape."""
+    from tklab.kernels.flash_attention import _launch_forward, check_device_status
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak = _peaks().get("bf16_tflops")
+    shapes = [(4, 16, 4096, 256), (2, 16, 8192, 256), (4, 16, 4096, 192)]
+    for batch, heads, seq, d in shapes:
+        for causal in (True, False):
+            q, k, v, _ = _make_inputs((batch, heads, seq, d), torch.bfloat16, 1.0, args.seed, device)
+            o = torch.empty_like(q)
+            lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=device)
+            for _ in range(args.warmup):
+                _launch_forward(q, k, v, o, lse, causal=causal, store_lse=True)
+            torch.cuda.synchronize(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                _launch_forward(q, k, v, o, lse, causal=causal, store_lse=True)
+            e1.record()
+            torch.cuda.synchronize(device)
+            ms = e0.elapsed_time(e1) / args.steps
+            tflops = fwd_flops(batch, heads, seq, d, causal) / (ms * 1e-3) / 1e12
+            print(json.dumps({
+                "wide_head_forward": True, "B": batch, "H": heads, "S": seq, "D": d, "causal": causal,
+                "dtype": "bf16", "ms": round(ms, 4), "tflops": round(tflops, 1),
+                "frac_of_measured_bf16": round(tflops / peak, 3) if peak else None,
+                "kernel": "attn_fwd_d256_kernel (256 columns; D < 256 zero-filled)",
+            }), flush=True)
+            del q, k, v, o, lse
+    check_device_status()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -698,6 +736,8 @@ def main() -> None:
                         help="GQA decode at the reference model's shapes, one JSON line per shape (1 GPU)")
     parser.add_argument("--rope", action="store_true",
                         help="fused RoPE attention vs plain and unfused, one JSON line per measurement (1 GPU)")
+    parser.add_argument("--wide", action="store_true",
+                        help="forward for head_dim 192/256 (the 256-column kernel), one JSON line per shape (1 GPU)")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
@@ -707,6 +747,8 @@ def main() -> None:
         run_rope(args)
     elif args.decode:
         run_decode(args)
+    elif args.wide:
+        run_wide(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

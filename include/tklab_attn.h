@@ -63,9 +63,10 @@ extern "C" {
 /* Forward attention.  o receives softmax(scale * q k^T) v (causal: key n
  * attends query m only when n <= m).  lse may be NULL; otherwise it
  * receives the base-2 log-sum-exp of every query row.  head_dim must be a
- * multiple of 8 from 8 to 128 (widths other than 64 and 128 run the 64- or
- * 128-column kernel with the missing columns zero-filled on load and clipped
- * on store); q, k, v, o must be 16-byte aligned. */
+ * multiple of 8 from 8 to 256 (widths other than 64, 128 and 256 run the
+ * next wider kernel with the missing columns zero-filled on load and clipped
+ * on store; 136..256 run the 256-column kernel, which has no backward); q,
+ * k, v, o must be 16-byte aligned. */
 TK_API int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
                 void* stream);
