@@ -45,8 +45,8 @@ def test_workspace_size_arithmetic() -> None:
     [
         ({"q": None}, 1),
         ({"head_dim": 100}, 2),
-        ({"head_dim": 136}, 2),
-        ({"head_dim": 256}, 2),
+        ({"head_dim": 260}, 2),
+        ({"head_dim": 264}, 2),
         ({"dtype": 7}, 2),
         ({"seq": 0}, 1),
         ({"batch": -1}, 1),
@@ -59,6 +59,16 @@ def test_forward_rejects_bad_arguments_before_launch(kwargs: dict, status: int) 
             "seq": 128, "head_dim": 64, "dtype": 0, "causal": 0, "scale": 0.125, "stream": None}
     args.update(kwargs)
     assert _native.load().tk_attn_fwd(*args.values()) == status
+
+
+@pytest.mark.parametrize("head_dim", [136, 256])
+def test_backward_rejects_wide_heads(head_dim: int) -> None:
+    """136..256 have a forward kernel only: every backward entry refuses them as unsupported."""
+    lib = _native.load()
+    p = 0x1000
+    assert lib.tk_attn_bwd_pre(p, p, p, p, 1, 2, 128, head_dim, 0, None) == 2
+    assert lib.tk_attn_bwd(p, p, p, p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
+    assert lib.tk_attn_bwd_deterministic(p, p, p, p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
 
 
 def test_backward_rejects_missing_workspace() -> None:
