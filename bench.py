@@ -641,6 +641,10 @@ def run_decode(args: argparse.Namespace) -> None:
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     shapes = [(1, 32, 8, 128, 4096), (1, 32, 8, 128, 131072), (32, 32, 8, 128, 4096), (64, 32, 8, 128, 8192),
               (16, 64, 8, 128, 16384)]
+    if args.shape:
+        if len(args.shape) != 5:
+            raise SystemExit("--decode --shape takes B,Hq,Hkv,Dh,L")
+        shapes = [tuple(args.shape)]
     for batch, hq, hkv, d, seq in shapes:
         g = torch.Generator(device=device).manual_seed(args.seed)
         q = torch.randn((batch, hq, d), generator=g, device=device).to(torch.float16)
@@ -688,8 +692,13 @@ def run_wide(args: argparse.Namespace) -> None:
     torch.cuda.set_device(device)
     peak = _peaks().get("bf16_tflops")
     shapes = [(4, 16, 4096, 256), (2, 16, 8192, 256), (4, 16, 4096, 192)]
+    causal_modes = (True, False)
+    if args.shape:
+        if len(args.shape) != 4:
+            raise SystemExit("--wide --shape takes B,H,S,D")
+        shapes, causal_modes = [tuple(args.shape)], (True,)
     for batch, heads, seq, d in shapes:
-        for causal in (True, False):
+        for causal in causal_modes:
             q, k, v, _ = _make_inputs((batch, heads, seq, d), torch.bfloat16, 1.0, args.seed, device)
             o = torch.empty_like(q)
             lse = torch.empty((batch, heads, seq), dtype=torch.float32, device=device)
@@ -738,6 +747,8 @@ def main() -> None:
                         help="fused RoPE attention vs plain and unfused, one JSON line per measurement (1 GPU)")
     parser.add_argument("--wide", action="store_true",
                         help="forward for head_dim 192/256 (the 256-column kernel), one JSON line per shape (1 GPU)")
+    parser.add_argument("--shape", type=lambda t: [int(x) for x in t.split(",")], default=None,
+                        help="one shape instead of the mode's list: --wide B,H,S,D (causal); --decode B,Hq,Hkv,Dh,L")
     args = parser.parse_args()
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
