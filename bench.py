@@ -633,14 +633,14 @@ def run_decode(args: argparse.Namespace) -> None:
     256 MiB write evicts L2 before every call) and warm (back-to-back calls).
     Reported against the model's minimum traffic (unique KV + Q + O bytes)
     and the measured HBM copy bandwidth; one JSON line per shape."""
-    from tklab.kernels.gqa_decode import decode_model, gqa_decode
+    from tklab.kernels.gqa_decode import decode_model, gqa_decode, set_decode_path
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     peaks = _peaks()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     shapes = [(1, 32, 8, 128, 4096), (1, 32, 8, 128, 131072), (32, 32, 8, 128, 4096), (64, 32, 8, 128, 8192),
-              (16, 64, 8, 128, 16384)]
+              (16, 64, 8, 128, 16384), (16, 128, 8, 128, 16384)]
     if args.shape:
         if len(args.shape) != 5:
             raise SystemExit("--decode --shape takes B,Hq,Hkv,Dh,L")
@@ -651,32 +651,43 @@ def run_decode(args: argparse.Namespace) -> None:
         k = torch.randn((batch, hkv, seq, d), generator=g, device=device).to(torch.float16)
         v = torch.randn((batch, hkv, seq, d), generator=g, device=device).to(torch.float16)
         model = decode_model(batch, hq, hkv, d, seq)
-        times = {}
+        tensor_cores = d == 128 and hq // hkv in (4, 8, 16)
+        # Both kernels where the tensor-core one applies, interleaved call by
+        # call so that clock and power drift hit them alike.
+        paths = ("auto", "cuda_cores") if tensor_cores else ("cuda_cores",)
+        samples = {(p, st): [] for p in paths for st in ("l2_flushed", "warm")}
         for state in ("l2_flushed", "warm"):
-            for _ in range(args.warmup):
-                gqa_decode(q, k, v)
-            samples = []
+            for path in paths:
+                set_decode_path(path)
+                for _ in range(args.warmup):
+                    gqa_decode(q, k, v)
             for _ in range(args.steps):
-                if state == "l2_flushed":
-                    flush.zero_()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                gqa_decode(q, k, v)
-                e1.record()
-                torch.cuda.synchronize(device)
-                samples.append(e0.elapsed_time(e1))
-            times[state] = statistics.median(samples)
-        ms = times["l2_flushed"]
-        gbs = model.bytes_min / (ms * 1e-3) / 1e9
-        print(json.dumps({
-            "decode": "gqa", "B": batch, "Hq": hq, "Hkv": hkv, "G": hq // hkv, "Dh": d, "L": seq,
-            "dtype": "float16", "ms_l2_flushed": round(ms, 4), "ms_warm": round(times["warm"], 4),
-            "bytes_min": model.bytes_min, "gbs_of_bytes_min": round(gbs, 1),
-            "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 3) if peaks.get("hbm_gbs") else None,
-            "useful_tflops": round(model.flops_useful / (ms * 1e-3) / 1e12, 2),
-            "intensity_min": round(model.intensity_min, 4),
-            "timing": "CUDA events, median; includes the split and combine kernels and the workspace allocation",
-        }), flush=True)
+                for path in paths:
+                    set_decode_path(path)
+                    if state == "l2_flushed":
+                        flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    gqa_decode(q, k, v)
+                    e1.record()
+                    torch.cuda.synchronize(device)
+                    samples[(path, state)].append(e0.elapsed_time(e1))
+        set_decode_path("auto")
+        for path in paths:
+            ms = statistics.median(samples[(path, "l2_flushed")])
+            warm = statistics.median(samples[(path, "warm")])
+            gbs = model.bytes_min / (ms * 1e-3) / 1e9
+            kernel = "tensor cores (tcgen05)" if path == "auto" else "CUDA cores"
+            print(json.dumps({
+                "decode": "gqa", "kernel": kernel, "B": batch, "Hq": hq, "Hkv": hkv, "G": hq // hkv, "Dh": d,
+                "L": seq,
+                "dtype": "float16", "ms_l2_flushed": round(ms, 4), "ms_warm": round(warm, 4),
+                "bytes_min": model.bytes_min, "gbs_of_bytes_min": round(gbs, 1),
+                "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 3) if peaks.get("hbm_gbs") else None,
+                "useful_tflops": round(model.flops_useful / (ms * 1e-3) / 1e12, 2),
+                "intensity_min": round(model.intensity_min, 4),
+                "timing": "CUDA events, median; includes the split and combine kernels and the workspace allocation",
+            }), flush=True)
         del q, k, v
 
 

@@ -175,13 +175,19 @@ TK_API int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float*
  *            or NULL for all seq_kv; a batch with none gets o = 0, lse = -inf
  *   lse      (batch, q_heads) fp32 base-2 log-sum-exp (scale included), or NULL
  *   o = softmax(q . K^T * scale) V over the valid keys.  G in {1, 2, 4, 8,
- *   16}, head_dim 64 or 128.  Split-KV: chunks of 64 keys per CTA (K and V
- *   by bulk copy into shared memory) and a combine pass; the partials live
- *   in `workspace`, at least tk_gqa_decode_workspace_bytes(...) bytes. */
+ *   16}, head_dim 64 or 128.  Split-KV with a combine pass; the partials live
+ *   in `workspace`, at least tk_gqa_decode_workspace_bytes(...) bytes.
+ *   head_dim 128 with G = 4, 8 or 16 runs the tensor-core kernel (128-key
+ *   tiles by TMA, S^T = K q^T and O^T = V^T P^T on tcgen05); the rest the
+ *   CUDA-core kernel (64-key chunks by bulk copy). */
 TK_API size_t tk_gqa_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t seq_kv, int64_t head_dim);
 TK_API int tk_gqa_decode(const void* q, const void* k, const void* v, const int32_t* kv_lens, void* o, float* lse,
                          void* workspace, size_t workspace_bytes, int64_t batch, int64_t q_heads,
                          int64_t kv_heads, int64_t seq_kv, int64_t head_dim, int dtype, float scale, void* stream);
+/* Process-wide choice of the decode kernel: -1 (default) tensor cores where
+ * supported, 0 always the CUDA-core kernel, 1 the same as -1.  For A/B
+ * measurements and tests; returns TK_ERR_INVALID_ARGUMENT otherwise. */
+TK_API int tk_gqa_decode_set_path(int mode);
 
 /* Bytes of the fp32 dQ accumulator tk_attn_bwd needs (0 on bad sizes). */
 TK_API size_t tk_attn_bwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim);

@@ -12,7 +12,7 @@ import torch
 
 from oracle import attention_oracle as orc
 from tklab.kernels.flash_attention import check_device_status
-from tklab.kernels.gqa_decode import decode_model, gqa_decode
+from tklab.kernels.gqa_decode import decode_model, gqa_decode, set_decode_path
 
 gpu = pytest.mark.skipif(not torch.cuda.is_available(), reason="CUDA GPU is required")
 
@@ -58,13 +58,26 @@ def test_decode_validation_on_cpu() -> None:
         gqa_decode(q, k, k)
 
 
+@pytest.fixture(params=["auto", "cuda_cores"])
+def decode_path(request: pytest.FixtureRequest):
+    """Run a test on both decode kernels (tensor cores where "auto" selects them)."""
+    set_decode_path(request.param)
+    yield request.param
+    set_decode_path("auto")
+
+
+def test_decode_path_validation() -> None:
+    with pytest.raises(ValueError, match="decode path"):
+        set_decode_path("tensor")
+
+
 @pytest.mark.gpu
 @gpu
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("group", [1, 2, 4, 8, 16])
 @pytest.mark.parametrize("head_dim", [64, 128])
-@pytest.mark.parametrize("seq", [1, 63, 64, 65, 1000, 4096])
-def test_decode_matches_oracle(dtype: torch.dtype, group: int, head_dim: int, seq: int) -> None:
+@pytest.mark.parametrize("seq", [1, 63, 64, 65, 127, 128, 129, 1000, 4096])
+def test_decode_matches_oracle(decode_path: str, dtype: torch.dtype, group: int, head_dim: int, seq: int) -> None:
     torch.manual_seed(seq + 3 * group + head_dim)
     batch, kv_heads = 2, 2
     q = torch.randn(batch, kv_heads * group, head_dim, device="cuda", dtype=dtype)
@@ -80,7 +93,7 @@ def test_decode_matches_oracle(dtype: torch.dtype, group: int, head_dim: int, se
 
 @pytest.mark.gpu
 @gpu
-def test_decode_ragged_lengths_and_4d_query() -> None:
+def test_decode_ragged_lengths_and_4d_query(decode_path: str) -> None:
     torch.manual_seed(9)
     batch, kv_heads, group, seq, dim = 5, 8, 4, 777, 128
     q = torch.randn(batch, kv_heads * group, 1, dim, device="cuda", dtype=torch.bfloat16)
@@ -100,6 +113,34 @@ def test_decode_ragged_lengths_and_4d_query() -> None:
     k2 = k.clone()
     k2[3, :, 64:] = 1e4
     assert torch.equal(gqa_decode(q, k2, v, kv_lens=lens), o)
+    check_device_status()
+
+
+@pytest.mark.gpu
+@gpu
+@pytest.mark.parametrize("group", [4, 16])
+def test_decode_tensor_core_path_agrees_with_cuda_cores(group: int) -> None:
+    """The two kernels on the same inputs (a long cache with many splits, growing scores so the
+    running maxima move often): equal to within the 16-bit rounding of P."""
+    torch.manual_seed(21 + group)
+    batch, kv_heads, seq, dim = 3, 4, 5000, 128
+    q = torch.randn(batch, kv_heads * group, dim, device="cuda", dtype=torch.bfloat16)
+    ramp = torch.linspace(0.1, 2.5, seq, device="cuda")[None, None, :, None]
+    k = (torch.randn(batch, kv_heads, seq, dim, device="cuda") * ramp).to(torch.bfloat16)
+    v = torch.randn(batch, kv_heads, seq, dim, device="cuda", dtype=torch.bfloat16)
+    try:
+        set_decode_path("cuda_cores")
+        o_cc, lse_cc = gqa_decode(q, k, v, return_lse=True)
+        set_decode_path("auto")
+        o_tc, lse_tc = gqa_decode(q, k, v, return_lse=True)
+        assert torch.equal(gqa_decode(q, k, v), o_tc)
+    finally:
+        set_decode_path("auto")
+    ref_o, ref_lse = orc.gqa_decode_reference(q, k, v)
+    assert (o_tc.float().cpu() - ref_o).abs().max().item() <= 1e-2
+    assert (o_tc.float() - o_cc.float()).abs().max().item() <= 1e-2
+    assert torch.allclose(lse_tc.cpu(), ref_lse, atol=1e-3, rtol=1e-4)
+    assert torch.allclose(lse_tc, lse_cc, atol=1e-3, rtol=1e-4)
     check_device_status()
 
 

@@ -21,6 +21,9 @@ constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {};
 std::mutex g_mu;
 unsigned long long g_timeout_ns = 2000000000ull;
+// GQA decode kernel choice: -1 tensor cores where supported (head_dim 128,
+// G = 4, 8 or 16), 0 always the CUDA-core kernel, 1 the same as -1.
+int g_decode_path = -1;
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -278,13 +281,31 @@ int tk_gqa_decode(const void* q, const void* k, const void* v, const int32_t* kv
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     return tk::kErrLaunch;
-  const int splits = tk::gqa_decode_splits(batch, kv_heads, seq_kv, sms);
+  const bool use_tc = g_decode_path != 0 && tk::gqa_decode_tc_supported(head_dim, group) &&
+                      batch * q_heads <= INT_MAX;
+  const int splits = use_tc ? tk::gqa_decode_splits_tc(batch, kv_heads, seq_kv, sms)
+                            : tk::gqa_decode_splits(batch, kv_heads, seq_kv, sms);
   float* part_o = static_cast<float*>(workspace);
   float* part_ml = part_o + batch * q_heads * splits * head_dim;
   tk::GqaDecodeArgs a{q, k, v, kv_lens, o, lse, part_o, part_ml, batch, kv_heads, group, seq_kv, head_dim,
                       splits, dtype == TK_DTYPE_BF16, scale * kLog2e, g_timeout_ns, status,
                       static_cast<cudaStream_t>(stream)};
+  CUtensorMap mq, mk, mv;
+  if (use_tc) {
+    if (int rc = make_map(&mq, q, 1, batch * q_heads, head_dim, dtype, 16)) return rc;
+    if (int rc = make_map(&mk, k, batch * kv_heads, seq_kv, head_dim, dtype)) return rc;
+    if (int rc = make_map(&mv, v, batch * kv_heads, seq_kv, head_dim, dtype)) return rc;
+    a.tm_q = &mq;
+    a.tm_k = &mk;
+    a.tm_v = &mv;
+  }
   return tk::launch_gqa_decode(a);
+}
+
+int tk_gqa_decode_set_path(int mode) {
+  if (mode < -1 || mode > 1) return tk::kErrInvalidArgument;
+  g_decode_path = mode;
+  return tk::kOk;
 }
 
 int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream) {

@@ -136,12 +136,19 @@ struct GqaDecodeArgs {
   float* part_o;       // workspace (B, Hkv * G, splits, D)
   float* part_ml;      // workspace (B, Hkv * G, splits, 2)
   int64_t B, Hkv, G, L, D;
-  int splits;  // from gqa_decode_splits
+  int splits;  // from gqa_decode_splits (CUDA cores) or gqa_decode_splits_tc (tensor cores)
   bool bf16;
   float scale_log2;
   unsigned long long timeout_ns;
   int* status;
   cudaStream_t stream;
+  // Tensor-core kernel (gqa_decode_tc_sm100.cu): maps over q as (B*Hq, D)
+  // rows with 16-row boxes and over K, V as (B*Hkv, L, D) with 128-row boxes;
+  // all nullptr selects the CUDA-core kernel.  Last, so positional
+  // initialisers of the fields above stay valid.
+  const CUtensorMap* tm_q = nullptr;
+  const CUtensorMap* tm_k = nullptr;
+  const CUtensorMap* tm_v = nullptr;
 };
 
 int launch_attn_fwd(const FwdArgs& a);
@@ -149,6 +156,9 @@ int launch_attn_fwd_d256(const FwdD256Args& a);
 int gqa_decode_splits(int64_t B, int64_t Hkv, int64_t L, int sm_count);
 int gqa_decode_keys_per_split(int64_t L, int n_splits);
 int launch_gqa_decode(const GqaDecodeArgs& a);
+bool gqa_decode_tc_supported(int64_t D, int64_t G);
+int gqa_decode_splits_tc(int64_t B, int64_t Hkv, int64_t L, int sm_count);
+int launch_gqa_decode_tc_split(const GqaDecodeArgs& a);
 int launch_rope_rotate(const RopeRotateArgs& a);
 int launch_dq_convert_rope(const DqConvertRopeArgs& a);
 int launch_attn_bwd_pre(const BwdPreArgs& a);

@@ -349,7 +349,9 @@ int launch_gqa_decode(const GqaDecodeArgs& a) {
   if (a.G < 1 || a.G > kDecMaxG) return kErrUnsupported;
   const int n_splits = a.splits;
   int rc;
-  if (a.D == 64)
+  if (a.tm_k != nullptr)
+    rc = launch_gqa_decode_tc_split(a);
+  else if (a.D == 64)
     rc = a.bf16 ? launch_d<64, true>(a, n_splits) : launch_d<64, false>(a, n_splits);
   else
     rc = a.bf16 ? launch_d<128, true>(a, n_splits) : launch_d<128, false>(a, n_splits);

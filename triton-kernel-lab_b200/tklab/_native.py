@@ -88,6 +88,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
             _i64, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_float, _vp,
         ],
     ),
+    "tk_gqa_decode_set_path": (ctypes.c_int, [ctypes.c_int]),
     "tk_attn_bwd_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64, _i64]),
     "tk_attn_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _vp]),
     "tk_attn_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_ulonglong]),

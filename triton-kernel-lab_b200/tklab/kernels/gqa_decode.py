@@ -5,9 +5,10 @@ The reference specifies contiguous GQA decode only as a model
 ``Hq = G * Hkv`` query heads, query head ``h`` reading KV head ``h // G``
 ("Semantic GQA mapping"), a contiguous KV cache ``(B, Hkv, L, Dh)``.
 :func:`gqa_decode` is the kernel for that workload (``tk_gqa_decode``:
-split-KV over chunks of 64 keys with a combine pass, K/V chunks brought into
-shared memory by bulk copies, CUDA-core arithmetic — the problem is
-HBM-bound at every practical G); :func:`decode_model` evaluates the model's
+split-KV with a combine pass; head_dim 128 with G = 4, 8 or 16 runs on the
+tensor cores — 128-key K/V tiles by TMA, S^T = K q^T and O^T = V^T P^T with
+tcgen05 — so the CUDA cores only run the softmax; other shapes use 64-key
+chunks by bulk copy and CUDA-core products); :func:`decode_model` evaluates the model's
 derived quantities (useful FLOPs, unique KV bytes, minimum traffic and the
 intensities) so measurements can be reported against it with the model's
 vocabulary kept distinct (useful vs executed work, payload-only vs minimum
@@ -26,6 +27,19 @@ from tklab.kernels.flash_attention import _NATIVE_DTYPE, _after_launch, _stream
 
 DECODE_GROUPS = (1, 2, 4, 8, 16)
 DECODE_HEAD_DIMS = (64, 128)
+DECODE_PATHS = {"auto": -1, "cuda_cores": 0}
+
+
+def set_decode_path(path: str) -> None:
+    """Choose the decode kernel for the whole process.
+
+    ``"auto"`` (default): tensor cores for head_dim 128 with G = 4, 8 or 16,
+    the CUDA-core kernel otherwise; ``"cuda_cores"``: always the CUDA-core
+    kernel (for A/B measurements and cross-checks).
+    """
+    if path not in DECODE_PATHS:
+        raise ValueError(f"decode path must be one of {tuple(DECODE_PATHS)}")
+    _native.check(_native.load().tk_gqa_decode_set_path(DECODE_PATHS[path]), "tk_gqa_decode_set_path")
 
 
 @dataclass(frozen=True, slots=True)
