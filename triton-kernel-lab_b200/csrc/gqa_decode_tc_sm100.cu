@@ -13,10 +13,12 @@
 //   heads (G padded with the following rows of q, whose columns are never
 //   read), K = 128 head-dim elements: 8 MMAs into one of two 16-column TMEM
 //   buffers.
-// * Softmax warps 4-7, thread t = key t of the tile: per-head tile maxima by
-//   warp butterflies and a 4-warp exchange through shared memory, base-2
-//   online softmax with the scale folded in and a lazy rescale (the running
-//   maximum moves only when a head's maximum grows by more than 2^8), row sums
+// * Softmax warps 4-7, thread t = key t of the tile: base-2 online softmax
+//   with the scale folded in.  The running maxima
+//   move only when some score of the tile lies more than 2^8 above its
+//   head's running maximum (one barrier with an OR reduction per tile
+//   decides); then the tile maxima come from a warp reduce-scatter and a
+//   4-warp exchange through shared memory and O is rescaled.  Row sums are
 //   kept per thread and reduced once at the end in a fixed order.  P^T is
 //   written as 16-bit values into shared memory (K-major, 16 head rows x 128
 //   keys, 128-byte swizzle), the B operand of
@@ -27,9 +29,11 @@
 //   query head go to the workspace in the format gqa_decode_combine_kernel
 //   merges.
 //
-// Every mbarrier wait is bounded; the softmax warps reach their named
-// barrier once per tile and once at the end whatever happens, so a timeout
-// never leaves a warp waiting on a barrier the others skipped.
+// Every mbarrier wait is bounded; the softmax warps reach the same named
+// barriers in every tile (whether a tile rescales is decided by a barrier
+// reduction, so it is the same in every warp) and once at the end whatever
+// happens, so a timeout never leaves a warp waiting on a barrier the others
+// skipped.
 #include "attn_launch.h"
 #include "sm100_primitives.cuh"
 
@@ -74,6 +78,42 @@ __device__ __forceinline__ uint16_t to16(float x) {
   } else {
     return __half_as_ushort(__float2half_rn(x));
   }
+}
+
+// Barrier over `threads` threads (named barrier `id`) that also returns
+// whether `pred` was true in any of them (bar.red.or).
+__device__ __forceinline__ bool named_barrier_or(int id, int threads, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(threads)
+      : "memory");
+  return out != 0;
+}
+
+// Maximum over the warp of each of G per-lane values, scattered: lane l
+// returns the maximum of value l / (32 / G).  A reduce-scatter (each step
+// sends half of the values still held and keeps the other half) followed by
+// plain butterflies: G - 1 + log2(32 / G) shuffles instead of 5 G.
+template <int G>
+__device__ __forceinline__ float warp_max_scatter(float (&v)[G], int lane) {
+#pragma unroll
+  for (int c = G, m = 16; c > 1; c >>= 1, m >>= 1) {
+    const bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < c / 2; ++i) {
+      const float send = upper ? v[i] : v[i + c / 2];
+      const float keep = upper ? v[i + c / 2] : v[i];
+      v[i] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, m));
+    }
+  }
+#pragma unroll
+  for (int m = 32 / G / 2; m > 0; m >>= 1) v[0] = fmaxf(v[0], __shfl_xor_sync(0xffffffffu, v[0], m));
+  return v[0];
 }
 
 template <int G, bool kBf16>
@@ -239,10 +279,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
-      // Every warp reaches the named barrier of every tile, failed or not.
+      // Every warp reaches the barriers of every tile, failed or not.
       ok = ok && warp_wait_tc(&s_full[j & 1], (j >> 1) & 1, ctl, timeout_ns, status, 7);
       float x[G];
-      float* red = sRed + (j & 1) * 4 * kTcN;
+      bool jump = false;
       if (ok) {
         tc_fence_after();
         uint32_t s[16];
@@ -251,55 +291,63 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         reg_fence16(s);
         const bool valid = first + j * kTcKeys + t < last;
 #pragma unroll
-        for (int g = 0; g < G; ++g) x[g] = valid ? __uint_as_float(s[g]) * scale_log2 : -INFINITY;
-        float wm[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) wm[g] = x[g];
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1)
-#pragma unroll
-          for (int g = 0; g < G; ++g) wm[g] = fmaxf(wm[g], __shfl_xor_sync(0xffffffffu, wm[g], off));
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-          if (lane == g) red[q4 * kTcN + g] = wm[g];
+        for (int g = 0; g < G; ++g) {
+          x[g] = valid ? __uint_as_float(s[g]) * scale_log2 : -INFINITY;
+          jump = jump || x[g] > m_run[g] + kTcRescale;
+        }
       }
-      named_barrier_sync(1, 128);
+      // Common case: no score of the tile is more than 2^8 above its head's
+      // running maximum, so P = 2^(x - m_run) as it is (no tile maximum, no
+      // exchange).  Otherwise (the first tile, or a head whose scores jumped)
+      // the tile maxima are computed and the running maxima moved.
+      const bool rescale = named_barrier_or(1, 128, jump);
+      float alpha[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) alpha[g] = 1.0f;
+      if (rescale) {
+        float* red = sRed + (j & 1) * 4 * kTcN;  // [head][warp]
+        if (ok) {
+          float wm[G];
+#pragma unroll
+          for (int g = 0; g < G; ++g) wm[g] = x[g];
+          const float hm = warp_max_scatter<G>(wm, lane);
+          if ((lane & (32 / G - 1)) == 0) red[(lane / (32 / G)) * 4 + q4] = hm;
+        }
+        named_barrier_sync(1, 128);
+        if (ok) {
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float4 w4 = *reinterpret_cast<const float4*>(red + g * 4);
+            const float m_new = fmaxf(m_run[g], fmaxf(fmaxf(w4.x, w4.y), fmaxf(w4.z, w4.w)));
+            alpha[g] = m_run[g] == -INFINITY ? 0.0f : ex2(m_run[g] - m_new);
+            m_run[g] = m_new;
+          }
+          if (j > 0) {
+            // P(j-1) V must be in O before O is rescaled.
+            ok = warp_wait_tc(pv_done, (j - 1) & 1, ctl, timeout_ns, status, 8);
+            if (ok) {
+              tc_fence_after();
+              uint32_t o[16];
+              tmem_ld16(t_lane + kColO, o);
+              tmem_wait_ld();
+              reg_fence16(o);
+#pragma unroll
+              for (int g = 0; g < G; ++g) o[g] = __float_as_uint(__uint_as_float(o[g]) * alpha[g]);
+              tmem_st16(t_lane + kColO, o);
+            }
+          }
+        }
+      }
       if (!ok) continue;
-      float m_use[G], alpha[G];
-      bool any = false;
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float tmax = fmaxf(fmaxf(red[g], red[kTcN + g]), fmaxf(red[2 * kTcN + g], red[3 * kTcN + g]));
-        const float m_new = fmaxf(m_run[g], tmax);
-        const bool need = m_new > m_run[g] + kTcRescale;
-        m_use[g] = need ? m_new : m_run[g];
-        alpha[g] = need ? (m_run[g] == -INFINITY ? 0.0f : ex2(m_run[g] - m_new)) : 1.0f;
-        any = any || need;
-      }
-      // (m_run and the tile maxima are the same in every thread: `any` is uniform.)
-      if (any && j > 0) {
-        // P(j-1) V must be in O before O is rescaled.
-        ok = warp_wait_tc(pv_done, (j - 1) & 1, ctl, timeout_ns, status, 8);
-        if (!ok) continue;
-        tc_fence_after();
-        uint32_t o[16];
-        tmem_ld16(t_lane + kColO, o);
-        tmem_wait_ld();
-        reg_fence16(o);
-#pragma unroll
-        for (int g = 0; g < G; ++g) o[g] = __float_as_uint(__uint_as_float(o[g]) * alpha[g]);
-        tmem_st16(t_lane + kColO, o);
-      }
       uint8_t* pbuf = sP + (j & 1) * kTcPBytes;
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float p = ex2(x[g] - m_use[g]);
+        const float p = ex2(x[g] - m_run[g]);
         lsum[g] = fmaf(lsum[g], alpha[g], p);
         *reinterpret_cast<uint16_t*>(pbuf + swz_offset(g, t, kTcN)) = to16<kBf16>(p);
-        m_run[g] = m_use[g];
       }
       fence_proxy_async_smem();
-      if (any && j > 0) tmem_wait_st();
+      if (rescale && j > 0) tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[j & 1]);
