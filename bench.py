@@ -752,7 +752,7 @@ def run_wide(args: argparse.Namespace) -> None:
                 "wide_head_forward": True, "B": batch, "H": heads, "S": seq, "D": d, "causal": causal,
                 "dtype": "bf16", "ms": round(ms, 4), "tflops": round(tflops, 1),
                 "frac_of_measured_bf16": round(tflops / peak, 3) if peak else None,
-                "kernel": "attn_fwd_d256_kernel (256 columns; D < 256 zero-filled)",
+                "kernel": "attn_fwd_d256_kernel (%d columns; D below it zero-filled)" % (192 if d <= 192 else 256),
             }), flush=True)
             del q, k, v, o, lse
     check_device_status()

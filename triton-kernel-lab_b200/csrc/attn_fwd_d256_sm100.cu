@@ -3,15 +3,16 @@
 // Same semantics as attn_fwd_sm100.cu (reference
 // src/tklab/kernels/flash_attention.py:54-117, :120-264: base-2 online
 // softmax with the scale folded in, P rounded to the input dtype for P.V,
-// O = acc / row_sum, LSE = m + log2(l)), laid out for a 256-column head:
+// O = acc / row_sum, LSE = m + log2(l)), laid out for a head of W = 192
+// (head dims 136..192) or 256 (200..256) columns:
 //
 // * One CTA = one 128-row query tile of one (batch, head); keys in tiles of
-//   64.  Tensor memory (512 columns): O [0,256), S in two 64-column buffers
+//   64.  Tensor memory (512 columns): O [0,W), S in two 64-column buffers
 //   [256,320) and [320,384) so S(j+1) runs while the softmax works on S(j);
 //   P(j) goes back packed over the first 32 columns of its S buffer and
-//   feeds the P.V MMA (M=128, N=256, K=16 per instruction) from TMEM.
-// * Shared memory: Q (64 KB, four 64-column blocks), K and V rings of two
-//   64-key stages (32 KB each): 192 KB.
+//   feeds the P.V MMA (M=128, N=W, K=16 per instruction) from TMEM.
+// * Shared memory: Q (W/64 blocks of 16 KB), K and V rings of two 64-key
+//   stages (W/64 blocks of 8 KB each): 192 KB at W = 256, 144 KB at 192.
 // * 8 warps: warp 0 TMA producer, warp 1 TMEM allocator and MMA issuer
 //   (converged warp, one elected lane issues), warps 4..7 softmax (thread t
 //   owns query row t = TMEM lane t) and epilogue.
@@ -19,29 +20,37 @@
 //   buffer P(j) was read from.  O is rescaled only when a row's running
 //   maximum moves by more than 2^8 (lazy rescale), and then after waiting
 //   for P(j-1).V to complete (pv_done).
-// * head_dim below 256 (a multiple of 8) runs this kernel with the tensor
-//   maps declaring the true width: loads zero-fill, the store clips.
+// * head_dim below W (a multiple of 8) runs the kernel with the tensor maps
+//   declaring the true width: loads zero-fill, the store clips.
 #include "attn_launch.h"
 #include "sm100_primitives.cuh"
 
 namespace tk {
 namespace {
 
-constexpr int kD256 = 256;
 constexpr int kKeyTile = 64;
 constexpr int kD256Threads = 256;
-constexpr int kQBytes = kTileRows * kD256 * 2;     // 64 KB
-constexpr int kKVBytes = kKeyTile * kD256 * 2;     // 32 KB
-constexpr int kKVBlockBytes = kKeyTile * kSwizzleBytes;  // 8 KB: one 64-column block of a key tile
-constexpr int kQOff = 0;
-constexpr int kKOff = kQOff + kQBytes;
-constexpr int kVOff = kKOff + 2 * kKVBytes;
-constexpr int kBarOff = kVOff + 2 * kKVBytes;
 // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2],
 // p_ready[2], pv_done, o_final
 constexpr int kNumBars = 1 + 8 + 2 + 2 + 2;
-constexpr int kCtlOff = kBarOff + kNumBars * 8;
-constexpr int kSmemBytes = kCtlOff + 64;
+
+// Layout for a kernel width of NB column blocks of 64 (NB = 3: head dims
+// 136..192, NB = 4: 200..256): shared memory Q (NB x 16 KB), K and V rings
+// of two 64-key stages (NB x 8 KB each); TMEM O in [0, 64 NB), S buffers at
+// columns 256 and 320.
+template <int NB>
+struct WideCfg {
+  static constexpr int kW = 64 * NB;
+  static constexpr int kQBytes = kTileRows * kW * 2;
+  static constexpr int kKVBytes = kKeyTile * kW * 2;
+  static constexpr int kQOff = 0;
+  static constexpr int kKOff = kQOff + kQBytes;
+  static constexpr int kVOff = kKOff + 2 * kKVBytes;
+  static constexpr int kBarOff = kVOff + 2 * kKVBytes;
+  static constexpr int kCtlOff = kBarOff + kNumBars * 8;
+  static constexpr int kSmemBytes = kCtlOff + 64;
+};
+constexpr int kKVBlockBytes = kKeyTile * kSwizzleBytes;  // 8 KB: one 64-column block of a key tile
 constexpr uint32_t kColO = 0;
 constexpr uint32_t kColS = 256;  // two buffers of 64 columns
 constexpr float kRescale = 8.0f;
@@ -52,7 +61,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaCon
   return __all_sync(0xffffffffu, ok);
 }
 
-template <bool kBf16>
+template <int NB, bool kBf16>
 __global__ void __launch_bounds__(kD256Threads, 1)
     attn_fwd_d256_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -72,10 +81,11 @@ __global__ void __launch_bounds__(kD256Threads, 1)
   const int n_ktiles = (S + kKeyTile - 1) / kKeyTile;
   const int n_kv = causal ? min((m0 + kTileRows + kKeyTile - 1) / kKeyTile, n_ktiles) : n_ktiles;
 
-  uint8_t* sQ = smem + kQOff;
-  uint8_t* sK = smem + kKOff;
-  uint8_t* sV = smem + kVOff;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  using C = WideCfg<NB>;
+  uint8_t* sQ = smem + C::kQOff;
+  uint8_t* sK = smem + C::kKOff;
+  uint8_t* sV = smem + C::kVOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* k_empty = k_full + 2;
@@ -85,7 +95,7 @@ __global__ void __launch_bounds__(kD256Threads, 1)
   uint64_t* p_ready = s_full + 2;
   uint64_t* pv_done = p_ready + 2;
   uint64_t* o_final = pv_done + 1;
-  CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + kCtlOff);
+  CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -117,22 +127,22 @@ __global__ void __launch_bounds__(kD256Threads, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer ----------------
-      mbar_arrive_expect_tx(q_full, kQBytes);
+      mbar_arrive_expect_tx(q_full, C::kQBytes);
 #pragma unroll
-      for (int b = 0; b < 4; ++b) tma_load_3d(sQ + b * kBlockBytes, &tm_q, q_full, b * 64, m0, bh);
+      for (int b = 0; b < NB; ++b) tma_load_3d(sQ + b * kBlockBytes, &tm_q, q_full, b * 64, m0, bh);
       for (int j = 0; j < n_kv; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1, ctl, timeout_ns, status, 1)) break;
-        mbar_arrive_expect_tx(&k_full[st], kKVBytes);
+        mbar_arrive_expect_tx(&k_full[st], C::kKVBytes);
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tma_load_3d(sK + st * kKVBytes + b * kKVBlockBytes, &tm_k, &k_full[st], b * 64, j * kKeyTile, bh);
+        for (int b = 0; b < NB; ++b)
+          tma_load_3d(sK + st * C::kKVBytes + b * kKVBlockBytes, &tm_k, &k_full[st], b * 64, j * kKeyTile, bh);
         if (!mbar_wait(&v_empty[st], ph ^ 1, ctl, timeout_ns, status, 2)) break;
-        mbar_arrive_expect_tx(&v_full[st], kKVBytes);
+        mbar_arrive_expect_tx(&v_full[st], C::kKVBytes);
 #pragma unroll
-        for (int b = 0; b < 4; ++b)
-          tma_load_3d(sV + st * kKVBytes + b * kKVBlockBytes, &tm_v, &v_full[st], b * 64, j * kKeyTile, bh);
+        for (int b = 0; b < NB; ++b)
+          tma_load_3d(sV + st * C::kKVBytes + b * kKVBlockBytes, &tm_v, &v_full[st], b * 64, j * kKeyTile, bh);
       }
     }
   } else if (warp == 1) {
@@ -140,11 +150,11 @@ __global__ void __launch_bounds__(kD256Threads, 1)
     const bool leader = elect_one();
     const uint32_t fmt = kBf16 ? 1u : 0u;
     const uint32_t idesc_s = idesc_f16(fmt, 128, kKeyTile, 0, 0);
-    const uint32_t idesc_pv = idesc_f16(fmt, 128, kD256, 0, 1);
+    const uint32_t idesc_pv = idesc_f16(fmt, 128, C::kW, 0, 1);
     const uint32_t q_lo = sdesc_lo_kmajor(smem_u32(sQ));
     const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(sK));
     const uint32_t v_lo0 = sdesc_lo_mnmajor(smem_u32(sV), kKeyTile);
-    constexpr uint32_t kStageLo = kKVBytes >> 4;
+    constexpr uint32_t kStageLo = C::kKVBytes >> 4;
     // S(j) = Q K_j^T into S buffer j&1 (16 MMAs of K = 16 over the 256 columns).
     auto issue_s = [&](int j) -> bool {
       const int st = j & 1;
@@ -153,7 +163,7 @@ __global__ void __launch_bounds__(kD256Threads, 1)
       if (leader) {
         const uint32_t k_lo = k_lo0 + st * kStageLo;
 #pragma unroll
-        for (int kk = 0; kk < kD256 / 16; ++kk)
+        for (int kk = 0; kk < C::kW / 16; ++kk)
           umma_ss_w(tmem + kColS + 64u * st, q_lo + kmajor_koff(kTileRows, kk * 16),
                     k_lo + kmajor_koff(kKeyTile, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit(&s_full[st]);
@@ -225,7 +235,7 @@ __global__ void __launch_bounds__(kD256Threads, 1)
         if (!(ok = warp_wait(pv_done, (j - 1) & 1, ctl, timeout_ns, status, 8))) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int cb = 0; cb < kD256 / 32; ++cb) {
+        for (int cb = 0; cb < C::kW / 32; ++cb) {
           uint32_t o[32];
           tmem_ld32(t_lane + kColO + cb * 32, o);
           tmem_wait_ld();
@@ -264,7 +274,7 @@ __global__ void __launch_bounds__(kD256Threads, 1)
       tc_fence_after();
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
 #pragma unroll 1
-      for (int cb = 0; cb < kD256 / 32; ++cb) {
+      for (int cb = 0; cb < C::kW / 32; ++cb) {
         uint32_t o[32];
         tmem_ld32(t_lane + kColO + cb * 32, o);
         tmem_wait_ld();
@@ -285,7 +295,7 @@ __global__ void __launch_bounds__(kD256Threads, 1)
     if (ok && q4 == 0 && lane == 0 && !ctl->abort) {
       // A store may clip a partial column block but never starts past the
       // tensor's true width.
-      for (int b = 0; b < 4 && b * 64 < d_real; ++b) tma_store_3d(&tm_o, sQ + b * kBlockBytes, b * 64, m0, bh);
+      for (int b = 0; b < NB && b * 64 < d_real; ++b) tma_store_3d(&tm_o, sQ + b * kBlockBytes, b * 64, m0, bh);
       tma_store_commit();
       tma_store_wait_read_all();
     }
@@ -301,32 +311,35 @@ __global__ void __launch_bounds__(kD256Threads, 1)
   }
 }
 
-template <bool kBf16>
+template <int NB, bool kBf16>
 int launch_d256_t(const FwdD256Args& a) {
-  static_assert(kSmemBytes <= 232448, "d256 forward shared memory exceeds the sm_100 limit");
-  auto kern = attn_fwd_d256_kernel<kBf16>;
+  using C = WideCfg<NB>;
+  static_assert(C::kSmemBytes <= 232448, "wide-head forward shared memory exceeds the sm_100 limit");
+  auto kern = attn_fwd_d256_kernel<NB, kBf16>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64) return kErrLaunch;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
       return kErrLaunch;
     attr_set[dev] = true;
   }
   const int n_qtiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
   const long long grid = static_cast<long long>(n_qtiles) * a.BH;
   if (grid > INT32_MAX) return kErrTooLarge;
-  kern<<<static_cast<unsigned>(grid), kD256Threads, kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), n_qtiles, a.causal, static_cast<int>(a.D), a.scale_log2,
-      a.timeout_ns, a.status);
+  kern<<<static_cast<unsigned>(grid), kD256Threads, C::kSmemBytes, a.stream>>>(
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, a.lse, static_cast<int>(a.S), n_qtiles, a.causal, static_cast<int>(a.D),
+      a.scale_log2, a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace
 
 int launch_attn_fwd_d256(const FwdD256Args& a) {
-  return a.bf16 ? launch_d256_t<true>(a) : launch_d256_t<false>(a);
+  if (a.D > 256) return kErrUnsupported;
+  if (a.D <= 192) return a.bf16 ? launch_d256_t<3, true>(a) : launch_d256_t<3, false>(a);
+  return a.bf16 ? launch_d256_t<4, true>(a) : launch_d256_t<4, false>(a);
 }
 
 }  // namespace tk

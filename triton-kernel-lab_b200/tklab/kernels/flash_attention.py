@@ -16,9 +16,10 @@ Contract differences from the reference, all widenings:
 * head_dim any multiple of 8 from 8 to 128 (reference: 64 only,
   ``:283-284``); widths below 64 / 128 run the 64- / 128-column kernels with
   the tensor maps declaring the true width;
-* forward only, head_dim 136 to 256 (multiples of 8) on a 256-column kernel
-  (one 128-row query tile per CTA against 64-key tiles); the backward of
-  those widths raises ``NotImplementedError``.
+* forward only, head_dim 136 to 256 (multiples of 8) on a 192-column
+  (136..192) or 256-column (200..256) kernel (one 128-row query tile per CTA
+  against 64-key tiles); the backward of those widths raises
+  ``NotImplementedError``.
 """
 
 from __future__ import annotations
