@@ -1,5 +1,5 @@
-"""GPU: the forward for head dims 136..256 (a 256-column kernel, 64-key tiles) against fp32 SDPA,
-and the backward's refusal of those widths.
+"""GPU: the forward for head dims 136..256 (persistent 192- and 256-column kernels, 64-key tiles)
+against fp32 SDPA, and the backward's refusal of those widths.
 """
 
 from __future__ import annotations
@@ -54,6 +54,31 @@ def test_wide_head_forward_matches_sdpa(dtype: torch.dtype, head_dim: int, causa
     assert (output.float() - reference).abs().max().item() <= 2e-2
     expected = _expected_lse(q, k, causal)
     assert (lse - expected).abs().max().item() <= 1e-3 * max(1.0, expected.abs().max().item())
+    check_device_status()
+
+
+@pytest.mark.gpu
+@gpu
+@pytest.mark.parametrize("head_dim", [176, 256])
+@pytest.mark.parametrize("causal", [False, True])
+def test_wide_head_forward_many_units_per_cta(head_dim: int, causal: bool) -> None:
+    """Enough (batch, head) slabs that every persistent CTA walks several work units, with an odd
+    number of query tiles (1100 rows: 9 tiles, the middle one an unpaired causal unit)."""
+    torch.manual_seed(17 + head_dim + int(causal))
+    shape = (2, 48, 1100, head_dim)
+    q, k, v = (torch.randn(shape, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    output = torch.full_like(q, float("nan"))
+    lse = torch.full(shape[:3], float("nan"), device="cuda")
+    _launch_forward(q, k, v, output, lse, causal=causal, store_lse=True)
+    reference = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
+    assert torch.isfinite(output).all()
+    assert_relative_frobenius(output, reference, max_relative_error=2e-2)
+    assert (output.float() - reference).abs().max().item() <= 3e-2
+    expected = _expected_lse(q, k, causal)
+    assert (lse - expected).abs().max().item() <= 1e-3 * max(1.0, expected.abs().max().item())
+    again = torch.empty_like(q)
+    _launch_forward(q, k, v, again, lse, causal=causal, store_lse=True)
+    assert torch.equal(again, output)
     check_device_status()
 
 

@@ -135,8 +135,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse
     if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
     if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype, 64)) return rc;
     if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype, 64)) return rc;
-    if (int rc = make_map(&mo, o, bh, seq, head_dim, dtype)) return rc;
-    tk::FwdD256Args a{&mq, &mk, &mv, &mo, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0,
+    tk::FwdD256Args a{&mq, &mk, &mv, o, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0,
                       scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
     return tk::launch_attn_fwd_d256(a);
   }

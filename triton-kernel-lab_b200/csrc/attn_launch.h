@@ -29,13 +29,14 @@ struct FwdArgs {
   const float* rope_sin = nullptr;
 };
 
-// Forward for 128 < head_dim <= 256 (attn_fwd_d256_sm100.cu): Q and O maps
-// with 128-row boxes, K and V maps with 64-row boxes.
+// Forward for 128 < head_dim <= 256 (attn_fwd_d256_sm100.cu): a Q map with
+// 128-row boxes, K and V maps with 64-row boxes; O (B*H, S, D) 16-bit is
+// stored directly.
 struct FwdD256Args {
   const CUtensorMap* tm_q;
   const CUtensorMap* tm_k;
   const CUtensorMap* tm_v;
-  const CUtensorMap* tm_o;
+  void* o;
   float* lse;
   int64_t BH, S, D;
   bool bf16;
