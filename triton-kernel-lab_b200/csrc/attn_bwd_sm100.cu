@@ -61,8 +61,8 @@ struct BwdCfg {
   static constexpr int kBarOff = kDeltaOff + 2 * 128 * 4;
   // kv_full, q_full[2], q_empty[2], do_full, do_empty, ld_full[2], ld_empty[2],
   // s_full, dp_full, p_ready, ds_ready, ds_empty, dq_full, dq_empty,
-  // stage_full, stage_free, dkdv_done
-  static constexpr int kNumBars = 1 + 4 + 2 + 4 + 10;
+  // stage_full[2], stage_free[2] (one per staging box), dkdv_done
+  static constexpr int kNumBars = 1 + 4 + 2 + 4 + 12;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -214,9 +214,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* ds_empty = ds_ready + 1;
   uint64_t* dq_full = ds_empty + 1;
   uint64_t* dq_empty = dq_full + 1;
-  uint64_t* stage_full = dq_empty + 1;
-  uint64_t* stage_free = stage_full + 1;
-  uint64_t* dkdv_done = stage_free + 1;
+  uint64_t* stage_full = dq_empty + 1;  // [2]
+  uint64_t* stage_free = stage_full + 2;  // [2]
+  uint64_t* dkdv_done = stage_free + 2;
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
@@ -236,8 +236,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(ds_empty, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
-    mbar_init(stage_full, 4);
-    mbar_init(stage_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&stage_full[i], 4);
+      mbar_init(&stage_free[i], 1);
+    }
     mbar_init(dkdv_done, 1);
     ctl->abort = 0;
     fence_mbarrier_init();
@@ -412,29 +414,40 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (ok) commit(dkdv_done);
     } else if (warp == 2 && kWithDq) {
       // ---------------- dQ reduce issuer ----------------
+      // Box by box: each 32-column box is reduced as soon as it is staged,
+      // and released once the TMA has read it (checked one reduction later,
+      // so that a box is being read while the other is being filled).
       bool ok = true;
+      int prev = -1;
       for (int it = 0; ok && it < n_steps; ++it) {
         const int m0 = (i_start + it) * kTileRows;
 #pragma unroll
         for (int pass = 0; pass < C::kDqPasses; ++pass) {
           const uint32_t cnt = static_cast<uint32_t>(it * C::kDqPasses + pass);
-          if (!(ok = warp_wait(stage_full, cnt & 1, ctl, timeout_ns, status, 18))) break;
-          if (lane == 0) {
 #pragma unroll
-            for (int bx = 0; bx < 2; ++bx) {
+          for (int bx = 0; bx < 2; ++bx) {
+            if (!(ok = warp_wait(&stage_full[bx], cnt & 1, ctl, timeout_ns, status, 18))) break;
+            if (lane == 0) {
               // A head_dim below the kernel's width leaves whole boxes past
-              // the tensor's last column: nothing to add there.
+              // the tensor's last column: nothing to add there (the group
+              // stays, empty, so that the count of groups in flight holds).
               if (pass * 64 + bx * 32 < d_real)
                 tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
+              tma_store_commit();
+              tma_store_wait_read_le1();
+              if (prev >= 0) mbar_arrive(&stage_free[prev]);
             }
-            tma_store_commit();
-            tma_store_wait_read_all();
-            mbar_arrive(stage_free);
+            prev = bx;
+            __syncwarp();
           }
-          __syncwarp();
+          if (!ok) break;
         }
       }
-      if (lane == 0) tma_store_wait_all();
+      if (lane == 0) {
+        tma_store_wait_read_all();
+        if (ok && prev >= 0) mbar_arrive(&stage_free[prev]);
+        tma_store_wait_all();
+      }
     }
   } else if (wg == 1) {
     warpgroup_reg_inc<kRegsDq>();
@@ -458,9 +471,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
       for (int pass = 0; pass < C::kDqPasses; ++pass) {
         const uint32_t cnt = static_cast<uint32_t>(it * C::kDqPasses + pass);
-        if (!(ok = warp_wait(stage_free, (cnt & 1) ^ 1, ctl, timeout_ns, status, 17))) break;
 #pragma unroll
         for (int bx = 0; bx < 2; ++bx) {
+          if (!(ok = warp_wait(&stage_free[bx], (cnt & 1) ^ 1, ctl, timeout_ns, status, 17))) break;
           uint8_t* box = sDQ + bx * kTileRows * kSwizzleBytes;
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
@@ -470,10 +483,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                                          __uint_as_float(v[pass * 2 + bx][ch * 4 + 3]) * scale);
             *reinterpret_cast<float4*>(box + swz_offset_f32(r, ch * 4)) = w;
           }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&stage_full[bx]);
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(stage_full);
+        if (!ok) break;
       }
     }
   } else {
