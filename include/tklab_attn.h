@@ -96,13 +96,14 @@ TK_API int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const 
                              int dtype, int causal, float scale, void* stream);
 TK_API int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dtype, void* stream);
 
-/* The backward for callers that cannot allocate device memory (code inside a
- * fixed-memory graph capture, frameworks that own every device byte through
+/* The backward for callers that cannot allocate device memory (plugins whose
+ * host gives them no allocator, frameworks that own every device byte through
  * their own pool, allocation-free hot loops).  Same inputs and outputs as
  * tk_attn_bwd_pre + tk_attn_bwd, but delta and the fp32 dQ accumulator live
  * in a 64 MiB array compiled into the library instead of caller buffers, so
- * nothing is allocated.  Limit: batch*heads*seq*(head_dim+1) <= 16,777,216,
- * else TK_ERR_TOO_LARGE before any launch.  The array is shared by all calls
+ * nothing is allocated.  head_dim 64 or 128.  Limit:
+ * batch*heads*seq*(head_dim+1) <= 16,777,216, else TK_ERR_TOO_LARGE before
+ * any launch.  The array is shared by all calls
  * on a device: calls whose kernels overlap on the GPU race on it; each call
  * clears the accumulator it needs.  The first call on a device looks up the
  * array's device address — make it before any stream capture.  Every GPU

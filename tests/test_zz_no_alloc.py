@@ -1,9 +1,8 @@
 """GPU: the allocation-free backward entry point, ``tk_attn_bwd_noalloc``.
 
 Some callers cannot allocate device memory at the point where they run the
-backward — code being captured into a CUDA graph with a fixed memory plan, a
-host framework whose pool owns every device byte, an allocation-free hot
-loop — so they cannot hand the regular backward its two scratch buffers
+backward — a plugin whose host gives it no allocator, a host framework whose
+pool owns every device byte, an allocation-free hot loop — so they cannot hand the regular backward its two scratch buffers
 (delta and the fp32 dQ accumulator).  ``tk_attn_bwd_noalloc`` keeps that
 scratch in a 64 MiB array inside the library instead.  This file checks,
 through the C ABI, that two calls in a row (different inputs, so the second

@@ -2,14 +2,15 @@
 // allocate device memory.
 //
 // Who needs it: code that runs where cudaMalloc is off limits or unsafe —
-// inside a region being captured into a CUDA graph with a fixed memory plan,
-// under a host framework that owns every device byte through its own pool
-// and forbids other allocations, or in a latency-critical loop where an
+// under a host framework or runtime that owns every device byte through its
+// own pool and forbids allocations behind its back, inside a plugin whose
+// host gives it no allocator, or in a latency-critical loop where an
 // allocation could synchronise the device.  The regular backward
 // (tk_attn_bwd_pre + tk_attn_bwd) needs two scratch buffers from the caller:
 // delta (B*H*S floats) and the fp32 dQ accumulator (B*H*S*D floats).  This
 // entry point takes the same inputs and outputs but keeps that scratch in a
-// fixed array compiled into the library, so it allocates nothing.
+// fixed array compiled into the library, so it allocates nothing.  It
+// accepts head_dim 64 or 128.
 //
 // Limits and sharing:
 //   * capacity: kScratchFloats = 16 Mi floats (64 MiB).  A problem fits when
