@@ -45,7 +45,7 @@ L2_FLUSH_BYTES = 256 << 20
 # (dram__bytes_read.sum + dram__bytes_write.sum) of the 64-slab case:
 # 404.8 MB + 223.9 MB over 64 slabs.  Traffic grows in proportion to the
 # slab count.
-BWD_DRAM_BYTES_PER_SLAB_C3 = 628.68e6 / 64
+BWD_DRAM_BYTES_PER_SLAB_C3 = 629.63e6 / 64
 THROTTLE_REASONS = {
     0x1: "gpu_idle",
     0x2: "applications_clocks_setting",
