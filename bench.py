@@ -349,32 +349,63 @@ def run_ours(args: argparse.Namespace) -> None:
 
 
 def _e2e(args, attn, shape, dtype, qk_std, device, rank, world) -> dict | None:
-    """Public API, pinned host buffers in, results (O, dQ, dK, dV) back to the host, per step."""
+    """Public API, pinned host buffers in, results (O, dQ, dK, dV) back to the host, every step.
+
+    The copies of consecutive steps overlap, as in a streaming pipeline: step
+    k's inputs go up on a copy stream into one of two device input sets (a set
+    is reused once the compute that read it has finished), the public call
+    runs on the compute stream, and step k's results come down on a third
+    stream while step k+1 computes and step k+2 uploads.  Every step still
+    moves its full inputs in and its full results out inside the timed region.
+    """
     b, h, s, d, _, causal, _ = CONFIGS[args.config]
     host_in = [t.cpu().pin_memory() for t in _make_inputs(shape, dtype, qk_std, seed=args.seed + 100 + rank,
                                                            device=device)]
     host_out = [torch.empty(shape, dtype=dtype).pin_memory() for _ in range(4)]
-    stream = torch.cuda.current_stream(device)
+    dev_in = [[torch.empty(shape, dtype=dtype, device=device) for _ in range(4)] for _ in range(2)]
+    compute = torch.cuda.current_stream(device)
+    up = torch.cuda.Stream(device)
+    down = torch.cuda.Stream(device)
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    for ev in in_free:
+        ev.record(compute)
 
-    def one() -> None:
-        q, k, v, do = (t.to(device, non_blocking=True) for t in host_in)
-        for t in (q, k, v):
-            t.requires_grad_(True)
+    def one(step: int) -> torch.cuda.Event:
+        slot = dev_in[step % 2]
+        up.wait_event(in_free[step % 2])
+        with torch.cuda.stream(up):
+            for dst, src in zip(slot, host_in, strict=True):
+                dst.copy_(src, non_blocking=True)
+        uploaded = torch.cuda.Event()
+        uploaded.record(up)
+        compute.wait_event(uploaded)
+        q, k, v = (t.detach().requires_grad_(True) for t in slot[:3])
         out = attn(q, k, v)
-        grads = torch.autograd.grad(out, (q, k, v), grad_outputs=do)
-        for dst, src in zip(host_out, (out, *grads), strict=True):
-            dst.copy_(src.detach(), non_blocking=True)
+        grads = torch.autograd.grad(out, (q, k, v), grad_outputs=slot[3])
+        in_free[step % 2].record(compute)
+        down.wait_stream(compute)
+        with torch.cuda.stream(down):
+            for dst, src in zip(host_out, (out, *grads), strict=True):
+                dst.copy_(src.detach(), non_blocking=True)
+        for t in (out, *grads):
+            t.record_stream(down)
+        downloaded = torch.cuda.Event()
+        downloaded.record(down)
+        return downloaded
 
-    for _ in range(max(1, args.warmup)):
-        one()
+    for i in range(max(1, args.warmup)):
+        one(i)
     torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.e2e_steps):
-        one()
-    end.record(stream)
+    start.record(compute)
+    up.wait_stream(compute)
+    last = None
+    for i in range(args.e2e_steps):
+        last = one(i)
+    compute.wait_event(last)
+    end.record(compute)
     torch.cuda.synchronize(device)
     ms = torch.tensor([start.elapsed_time(end) / args.e2e_steps], dtype=torch.float64, device=device)
     if world > 1:
@@ -388,7 +419,8 @@ def _e2e(args, attn, shape, dtype, qk_std, device, rank, world) -> dict | None:
         "ms_per_step": round(ms_step, 3),
         "h2d_bytes_per_step": per_rank_bytes * world,
         "d2h_bytes_per_step": per_rank_bytes * world,
-        "path": "tklab.kernels.flash_attention.attention_causal + torch.autograd.grad, pinned host buffers",
+        "path": "tklab.kernels.flash_attention.attention_causal + torch.autograd.grad, pinned host buffers; "
+                "uploads, compute and downloads of consecutive steps overlap on three streams",
         "steps": args.e2e_steps,
     }
 
@@ -766,7 +798,7 @@ def main() -> None:
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--config", choices=tuple(CONFIGS), default="c3")
     parser.add_argument("--seed", type=int, default=0)
-    parser.add_argument("--e2e-steps", type=int, default=5)
+    parser.add_argument("--e2e-steps", type=int, default=10)
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
