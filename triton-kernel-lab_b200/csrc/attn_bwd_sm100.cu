@@ -123,9 +123,10 @@ __device__ __forceinline__ void stage_row(uint32_t t_row, uint8_t* tile, int r, 
 // Of the 16 exponential pairs of an unmasked 32-query chunk, the pairs of
 // this many 4-query groups (two pairs each) run on the FMA pipe
 // (exp2_fma_pair): with both dS warpgroups in their P phase the MUFU
-// (16 exp2/clk/SM) would otherwise bound it.
+// (16 exp2/clk/SM) would otherwise bound it.  2 of 8 measured best with the
+// box-by-box dQ staging (1 and 3 were 1-2 % and 3-4 % slower end to end).
 #ifndef TK_BWD_EMU_GROUPS_PER8
-#define TK_BWD_EMU_GROUPS_PER8 3
+#define TK_BWD_EMU_GROUPS_PER8 2
 #endif
 constexpr int kBwdEmuGroupsPer8 = TK_BWD_EMU_GROUPS_PER8;
 
