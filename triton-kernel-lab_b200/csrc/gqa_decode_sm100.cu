@@ -237,6 +237,9 @@ __global__ void __launch_bounds__(kDecThreads)
     // sK, sV and sS are reused by the next sub-chunk.
     __syncthreads();
   }
+  // The combine kernel may start launching; it reads the partials only after
+  // this grid has completed.
+  pdl_launch_dependents();
   if (!ok || first >= last) {
     // Failed copy, or no keys (past this batch's length): a neutral partial
     // (m = -inf, l = 0, o = 0).
@@ -275,6 +278,9 @@ __global__ void __launch_bounds__(128)
     gqa_decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                               uint16_t* __restrict__ out, float* __restrict__ lse, long long n_heads, int n_splits) {
   constexpr int kCols = D / 32;
+  // Launched as a programmatic dependent of the split kernel: wait for its
+  // partials before reading them.
+  pdl_wait_prerequisites();
   const long long head = static_cast<long long>(blockIdx.x) * 4 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (head >= n_heads) return;
@@ -300,6 +306,26 @@ __global__ void __launch_bounds__(128)
   for (int c = 0; c < kCols; c += 2)
     *reinterpret_cast<uint32_t*>(out + head * D + lane * kCols + c) = pack2<kBf16>(acc[c] * inv, acc[c + 1] * inv);
   if (lse != nullptr && lane == 0) lse[head] = (l > 0.0f) ? m + lg2(l) : -INFINITY;
+}
+
+// The combine kernel as a programmatic dependent launch: its CTAs may be
+// scheduled while the split kernel's last CTAs finish, hiding the launch
+// latency (it waits for the split grid to complete before reading).
+template <int D, bool kBf16>
+cudaError_t launch_combine(const GqaDecodeArgs& a, unsigned blocks, long long n_heads, int n_splits) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = a.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gqa_decode_combine_kernel<D, kBf16>, static_cast<const float*>(a.part_o),
+                            static_cast<const float*>(a.part_ml), static_cast<uint16_t*>(a.o), a.lse, n_heads,
+                            n_splits);
 }
 
 template <int D, int G, bool kBf16>
@@ -358,26 +384,14 @@ int launch_gqa_decode(const GqaDecodeArgs& a) {
   if (rc != kOk) return rc;
   const long long n_heads = a.B * a.Hkv * a.G;
   const unsigned blocks = static_cast<unsigned>((n_heads + 3) / 4);
-  if (a.D == 64) {
-    if (a.bf16)
-      gqa_decode_combine_kernel<64, true><<<blocks, 128, 0, a.stream>>>(a.part_o, a.part_ml,
-                                                                         static_cast<uint16_t*>(a.o), a.lse, n_heads,
-                                                                         n_splits);
-    else
-      gqa_decode_combine_kernel<64, false><<<blocks, 128, 0, a.stream>>>(a.part_o, a.part_ml,
-                                                                          static_cast<uint16_t*>(a.o), a.lse, n_heads,
-                                                                          n_splits);
-  } else {
-    if (a.bf16)
-      gqa_decode_combine_kernel<128, true><<<blocks, 128, 0, a.stream>>>(a.part_o, a.part_ml,
-                                                                          static_cast<uint16_t*>(a.o), a.lse,
-                                                                          n_heads, n_splits);
-    else
-      gqa_decode_combine_kernel<128, false><<<blocks, 128, 0, a.stream>>>(a.part_o, a.part_ml,
-                                                                           static_cast<uint16_t*>(a.o), a.lse,
-                                                                           n_heads, n_splits);
-  }
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+  cudaError_t err;
+  if (a.D == 64)
+    err = a.bf16 ? launch_combine<64, true>(a, blocks, n_heads, n_splits)
+                 : launch_combine<64, false>(a, blocks, n_heads, n_splits);
+  else
+    err = a.bf16 ? launch_combine<128, true>(a, blocks, n_heads, n_splits)
+                 : launch_combine<128, false>(a, blocks, n_heads, n_splits);
+  return err == cudaSuccess && cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 }  // namespace tk

@@ -352,6 +352,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[j & 1]);
     }
+    // The combine kernel may start launching; it reads the partials only
+    // after this grid has completed.
+    pdl_launch_dependents();
     // Row sums: warp butterflies, then the four warps in a fixed order.
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
