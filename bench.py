@@ -672,7 +672,7 @@ def run_decode(args: argparse.Namespace) -> None:
     peaks = _peaks()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     shapes = [(1, 32, 8, 128, 4096), (1, 32, 8, 128, 131072), (32, 32, 8, 128, 4096), (64, 32, 8, 128, 8192),
-              (16, 64, 8, 128, 16384), (16, 128, 8, 128, 16384)]
+              (16, 64, 8, 128, 16384), (16, 128, 8, 128, 16384), (16, 64, 8, 64, 16384)]
     if args.shape:
         if len(args.shape) != 5:
             raise SystemExit("--decode --shape takes B,Hq,Hkv,Dh,L")
@@ -683,7 +683,7 @@ def run_decode(args: argparse.Namespace) -> None:
         k = torch.randn((batch, hkv, seq, d), generator=g, device=device).to(torch.float16)
         v = torch.randn((batch, hkv, seq, d), generator=g, device=device).to(torch.float16)
         model = decode_model(batch, hq, hkv, d, seq)
-        tensor_cores = d == 128 and hq // hkv in (4, 8, 16)
+        tensor_cores = d in (64, 128) and hq // hkv in (4, 8, 16)
         # Both kernels where the tensor-core one applies, interleaved call by
         # call so that clock and power drift hit them alike.  Each kernel's
         # call is also captured in a CUDA graph: replaying it times the

@@ -178,7 +178,7 @@ TK_API int tk_attn_dq_convert_rope(const float* dq_accum, void* dq, const float*
  *   o = softmax(q . K^T * scale) V over the valid keys.  G in {1, 2, 4, 8,
  *   16}, head_dim 64 or 128.  Split-KV with a combine pass; the partials live
  *   in `workspace`, at least tk_gqa_decode_workspace_bytes(...) bytes.
- *   head_dim 128 with G = 4, 8 or 16 runs the tensor-core kernel (128-key
+ *   G = 4, 8 or 16 runs the tensor-core kernel (128-key
  *   tiles by TMA, S^T = K q^T and O^T = V^T P^T on tcgen05); the rest the
  *   CUDA-core kernel (64-key chunks by bulk copy). */
 TK_API size_t tk_gqa_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t seq_kv, int64_t head_dim);

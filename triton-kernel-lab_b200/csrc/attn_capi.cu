@@ -21,8 +21,8 @@ constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {};
 std::mutex g_mu;
 unsigned long long g_timeout_ns = 2000000000ull;
-// GQA decode kernel choice: -1 tensor cores where supported (head_dim 128,
-// G = 4, 8 or 16), 0 always the CUDA-core kernel, 1 the same as -1.
+// GQA decode kernel choice: -1 tensor cores where supported (G = 4, 8 or
+// 16), 0 always the CUDA-core kernel, 1 the same as -1.
 int g_decode_path = -1;
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {

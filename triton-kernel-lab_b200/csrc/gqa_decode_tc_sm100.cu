@@ -1,4 +1,6 @@
-// GQA decode with the products on the tensor cores (tcgen05), head_dim 128.
+// GQA decode with the products on the tensor cores (tcgen05), head_dim 64 or
+// 128 (the layout is sized for 128: at 64 only the first 64-column block of
+// each K, V and q tile is loaded).
 //
 // The same workload and partial format as gqa_decode_sm100.cu (one query
 // token per query head, G query heads per KV head, contiguous (B, Hkv, L, D)
@@ -41,7 +43,7 @@ namespace tk {
 namespace {
 
 constexpr int kTcKeys = 128;  // keys per tile (the M of S^T)
-constexpr int kTcD = 128;
+constexpr int kTcD = 128;  // shared-memory layout and O^T rows are sized for head_dim 128
 constexpr int kTcN = 16;  // query heads per MMA (G padded)
 constexpr int kTcStages = 3;
 constexpr int kTcThreads = 256;
@@ -116,13 +118,14 @@ __device__ __forceinline__ float warp_max_scatter(float (&v)[G], int lane) {
   return v[0];
 }
 
-template <int G, bool kBf16>
+template <int D, int G, bool kBf16>
 __global__ void __launch_bounds__(kTcThreads, 1)
     gqa_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const int* __restrict__ kv_lens,
                          float* __restrict__ part_o, float* __restrict__ part_ml, int Hkv, int L, int n_splits,
                          int keys_per_split, float scale_log2, unsigned long long timeout_ns, int* status) {
   static_assert(G >= 1 && G <= kTcN, "query heads per KV head must fit one MMA's N");
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) atomicCAS(status, kOk, kErrMisaligned);
@@ -199,18 +202,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint64_t* full = is_k ? k_full : v_full;
       uint64_t* empty = is_k ? k_empty : v_empty;
       if (is_k) {
-        mbar_arrive_expect_tx(q_full, kTcQBytes);
+        mbar_arrive_expect_tx(q_full, kTcN * D * 2);
 #pragma unroll
-        for (int blk = 0; blk < kTcD / 64; ++blk)
+        for (int blk = 0; blk < D / 64; ++blk)
           tma_load_3d(sQ + blk * kTcQBlockBytes, &tm_q, q_full, blk * 64, q_row0, 0);
       }
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % kTcStages;
         const uint32_t ph = (j / kTcStages) & 1;
         if (!mbar_wait(&empty[st], ph ^ 1, ctl, timeout_ns, status, is_k ? 1 : 2)) break;
-        mbar_arrive_expect_tx(&full[st], kTcTileBytes);
+        mbar_arrive_expect_tx(&full[st], kTcKeys * D * 2);
 #pragma unroll
-        for (int blk = 0; blk < kTcD / 64; ++blk)
+        for (int blk = 0; blk < D / 64; ++blk)
           tma_load_3d(ring + st * kTcTileBytes + blk * kTcBlockBytes, map, &full[st], blk * 64,
                       first + j * kTcKeys, kv_slab);
       }
@@ -221,6 +224,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const bool leader = elect_one();
       const uint32_t fmt = kBf16 ? 1u : 0u;
       const uint32_t idesc_s = idesc_f16(fmt, kTcKeys, kTcN, 0, 0);
+      // O^T has M = 128 rows for both head dims: at D = 64 the second
+      // 64-row block reads the unused half of the V stage (its rows of O^T
+      // are never read), which keeps the 128-lane accumulator layout.
       const uint32_t idesc_o = idesc_f16(fmt, kTcD, kTcN, 1, 0);
       const uint32_t q_lo = sdesc_lo_kmajor(smem_u32(sQ));
       const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(sK));
@@ -235,7 +241,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         if (leader) {
 #pragma unroll
-          for (int kk = 0; kk < kTcD / 16; ++kk)
+          for (int kk = 0; kk < D / 16; ++kk)
             umma_ss_w(tmem + 16u * (j & 1), k_lo0 + st * kStageLo + kmajor_koff(kTcKeys, kk * 16),
                       q_lo + kmajor_koff(kTcN, kk * 16), idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(&s_full[j & 1]);
@@ -372,7 +378,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tmem_wait_ld();
       reg_fence16(o);
 #pragma unroll
-      for (int g = 0; g < G; ++g) part_o[(part0 + static_cast<size_t>(g) * n_splits) * kTcD + t] = __uint_as_float(o[g]);
+      if (t < D)
+#pragma unroll
+        for (int g = 0; g < G; ++g) part_o[(part0 + static_cast<size_t>(g) * n_splits) * D + t] = __uint_as_float(o[g]);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         if (t == g) {
@@ -384,7 +392,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else {
       // No keys in this split, or a wait that ran out: a neutral partial.
 #pragma unroll
-      for (int g = 0; g < G; ++g) part_o[(part0 + static_cast<size_t>(g) * n_splits) * kTcD + t] = 0.0f;
+      if (t < D)
+#pragma unroll
+        for (int g = 0; g < G; ++g) part_o[(part0 + static_cast<size_t>(g) * n_splits) * D + t] = 0.0f;
       if (t < G) {
         part_ml[(part0 + static_cast<size_t>(t) * n_splits) * 2 + 0] = -INFINITY;
         part_ml[(part0 + static_cast<size_t>(t) * n_splits) * 2 + 1] = 0.0f;
@@ -401,10 +411,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-template <int G, bool kBf16>
+template <int D, int G, bool kBf16>
 int launch_tc_t(const GqaDecodeArgs& a, int n_splits, int keys_per_split) {
   static_assert(kTcSmemBytes <= 232448, "decode shared memory exceeds the sm_100 limit");
-  auto kern = gqa_decode_tc_kernel<G, kBf16>;
+  auto kern = gqa_decode_tc_kernel<D, G, kBf16>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -421,19 +431,19 @@ int launch_tc_t(const GqaDecodeArgs& a, int n_splits, int keys_per_split) {
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
-template <bool kBf16>
+template <int D, bool kBf16>
 int launch_tc_g(const GqaDecodeArgs& a, int n_splits, int keys_per_split) {
   switch (a.G) {
-    case 4: return launch_tc_t<4, kBf16>(a, n_splits, keys_per_split);
-    case 8: return launch_tc_t<8, kBf16>(a, n_splits, keys_per_split);
-    case 16: return launch_tc_t<16, kBf16>(a, n_splits, keys_per_split);
+    case 4: return launch_tc_t<D, 4, kBf16>(a, n_splits, keys_per_split);
+    case 8: return launch_tc_t<D, 8, kBf16>(a, n_splits, keys_per_split);
+    case 16: return launch_tc_t<D, 16, kBf16>(a, n_splits, keys_per_split);
     default: return kErrUnsupported;
   }
 }
 
 }  // namespace
 
-bool gqa_decode_tc_supported(int64_t D, int64_t G) { return D == kTcD && (G == 4 || G == 8 || G == 16); }
+bool gqa_decode_tc_supported(int64_t D, int64_t G) { return (D == 64 || D == 128) && (G == 4 || G == 8 || G == 16); }
 
 // Splits per (batch, KV head) for the tensor-core kernel (one CTA per SM):
 // the count that minimises a simple makespan model — waves of CTAs times
@@ -469,7 +479,8 @@ int launch_gqa_decode_tc_split(const GqaDecodeArgs& a) {
   if (!gqa_decode_tc_supported(a.D, a.G) || a.tm_q == nullptr || a.tm_k == nullptr || a.tm_v == nullptr)
     return kErrUnsupported;
   const int kps = gqa_decode_keys_per_split_tc(a.L, a.splits);
-  return a.bf16 ? launch_tc_g<true>(a, a.splits, kps) : launch_tc_g<false>(a, a.splits, kps);
+  if (a.D == 64) return a.bf16 ? launch_tc_g<64, true>(a, a.splits, kps) : launch_tc_g<64, false>(a, a.splits, kps);
+  return a.bf16 ? launch_tc_g<128, true>(a, a.splits, kps) : launch_tc_g<128, false>(a, a.splits, kps);
 }
 
 }  // namespace tk

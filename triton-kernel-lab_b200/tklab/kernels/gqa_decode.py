@@ -5,7 +5,7 @@ The reference specifies contiguous GQA decode only as a model
 ``Hq = G * Hkv`` query heads, query head ``h`` reading KV head ``h // G``
 ("Semantic GQA mapping"), a contiguous KV cache ``(B, Hkv, L, Dh)``.
 :func:`gqa_decode` is the kernel for that workload (``tk_gqa_decode``:
-split-KV with a combine pass; head_dim 128 with G = 4, 8 or 16 runs on the
+split-KV with a combine pass; G = 4, 8 or 16 runs on the
 tensor cores — 128-key K/V tiles by TMA, S^T = K q^T and O^T = V^T P^T with
 tcgen05 — so the CUDA cores only run the softmax; other shapes use 64-key
 chunks by bulk copy and CUDA-core products); :func:`decode_model` evaluates the model's
@@ -33,8 +33,8 @@ DECODE_PATHS = {"auto": -1, "cuda_cores": 0}
 def set_decode_path(path: str) -> None:
     """Choose the decode kernel for the whole process.
 
-    ``"auto"`` (default): tensor cores for head_dim 128 with G = 4, 8 or 16,
-    the CUDA-core kernel otherwise; ``"cuda_cores"``: always the CUDA-core
+    ``"auto"`` (default): tensor cores for G = 4, 8 or 16, the CUDA-core
+    kernel otherwise; ``"cuda_cores"``: always the CUDA-core
     kernel (for A/B measurements and cross-checks).
     """
     if path not in DECODE_PATHS:
