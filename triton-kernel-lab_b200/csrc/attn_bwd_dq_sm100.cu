@@ -51,10 +51,10 @@ struct DqCfg {
   static constexpr int kVOff = kKOff + kKStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kVStages * kTileBytes;
   // qdo_full, kv_full[KS], k_empty[KS], v_empty[VS], sdp_full, sdp_free,
-  // ds_ready, dq_done.  K_j and V_j land on one barrier, kv_full[j % KS]
+  // ds_ready[2], dq_done.  K_j and V_j land on one barrier, kv_full[j % KS]
   // (two producer arrivals plus both tiles' bytes), so the MMA warp polls
   // once per tile for its operands.
-  static constexpr int kNumBars = 1 + 2 * kKStages + kVStages + 4;
+  static constexpr int kNumBars = 1 + 2 * kKStages + kVStages + 5;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -113,8 +113,13 @@ __global__ void __launch_bounds__(kDqThreads, 1)
   uint64_t* v_empty = k_empty + C::kKStages;
   uint64_t* sdp_full = v_empty + C::kVStages;
   uint64_t* sdp_free = sdp_full + 1;
+  // ds_ready[2], by tile parity like the dS buffers it hands over: the MMA
+  // warp issues S/dP(t) before it takes dS(t-1), so the compute warps can
+  // finish tiles t-1 and t before it looks; one barrier would then be two
+  // phases ahead of its parity wait.  Tile t+2, the next user of
+  // ds_ready[t & 1], needs S/dP(t+2), issued only after dS(t) was taken.
   uint64_t* ds_ready = sdp_free + 1;
-  uint64_t* dq_done = ds_ready + 1;
+  uint64_t* dq_done = ds_ready + 2;
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
 
   if (threadIdx.x == 0) {
@@ -126,7 +131,8 @@ __global__ void __launch_bounds__(kDqThreads, 1)
     for (int i = 0; i < C::kVStages; ++i) mbar_init(&v_empty[i], 1);
     mbar_init(sdp_full, 1);
     mbar_init(sdp_free, 8);  // every warp of both compute warpgroups
-    mbar_init(ds_ready, 8);
+    mbar_init(&ds_ready[0], 8);
+    mbar_init(&ds_ready[1], 8);
     mbar_init(dq_done, 1);
     ctl->abort = 0;
     fence_mbarrier_init();
@@ -231,7 +237,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
           // dQ += dS(j) K_j with dS(j) packed in TMEM buffer j&1.
           const int j = t - 1;
           const int ks = j % C::kKStages;
-          if (!(ok = warp_wait(ds_ready, j & 1, ctl, timeout_ns, status, 7))) break;
+          if (!(ok = warp_wait(&ds_ready[j & 1], (j >> 1) & 1, ctl, timeout_ns, status, 7))) break;
           tc_fence_after();
           if (leader) {
             const uint32_t k_mn_lo = k_mn_lo0 + ks * kTileLo;
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(kDqThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(ds_ready);
+      if (lane == 0) mbar_arrive(&ds_ready[j & 1]);
     }
     // Epilogue: dQ * scale -> the input dtype, staged through the Q buffer
     // (dead once the last S product has completed, which dq_done implies);
