@@ -112,3 +112,20 @@ def test_deterministic_backward_c3_slabs() -> None:
     assert torch.isfinite(det[0]).all()
     assert relative_frobenius_error(det[0].float(), ref[0].float()) < 2e-3
     check_device_status()
+
+
+def test_deterministic_backward_repeated_long_sequences() -> None:
+    """Many back-to-back deterministic backwards over long sequences (K/V tile loads
+    that keep the dQ kernel's MMA warp waiting while its compute warps run ahead):
+    no bounded wait may expire (the device status stays clean) and every call returns
+    the same dQ bit for bit.  Guards the hand-over of dS between the compute warps and
+    the MMA warp, whose barrier once fell two phases behind in exactly this situation."""
+    torch.manual_seed(3)
+    shape = (2, 32, 4096, 128)
+    q, k, v, do = (torch.randn(shape, device="cuda", dtype=torch.bfloat16) for _ in range(4))
+    o, lse = _forward(q, k, v, True)
+    first = _launch_backward(q, k, v, o, lse, do, causal=True, deterministic=True)
+    for _ in range(24):
+        again = _launch_backward(q, k, v, o, lse, do, causal=True, deterministic=True)
+        assert torch.equal(again[0], first[0])
+    check_device_status()
