@@ -282,7 +282,7 @@ int tk_gqa_decode(const void* q, const void* k, const void* v, const int32_t* kv
     return tk::kErrLaunch;
   const bool use_tc = g_decode_path != 0 && tk::gqa_decode_tc_supported(head_dim, group) &&
                       batch * q_heads <= INT_MAX;
-  const int splits = use_tc ? tk::gqa_decode_splits_tc(batch, kv_heads, seq_kv, sms)
+  const int splits = use_tc ? tk::gqa_decode_splits_tc(batch, kv_heads, seq_kv, head_dim, sms)
                             : tk::gqa_decode_splits(batch, kv_heads, seq_kv, sms);
   float* part_o = static_cast<float*>(workspace);
   float* part_ml = part_o + batch * q_heads * splits * head_dim;

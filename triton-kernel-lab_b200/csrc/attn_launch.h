@@ -158,7 +158,7 @@ int gqa_decode_splits(int64_t B, int64_t Hkv, int64_t L, int sm_count);
 int gqa_decode_keys_per_split(int64_t L, int n_splits);
 int launch_gqa_decode(const GqaDecodeArgs& a);
 bool gqa_decode_tc_supported(int64_t D, int64_t G);
-int gqa_decode_splits_tc(int64_t B, int64_t Hkv, int64_t L, int sm_count);
+int gqa_decode_splits_tc(int64_t B, int64_t Hkv, int64_t L, int64_t D, int sm_count);
 int launch_gqa_decode_tc_split(const GqaDecodeArgs& a);
 int launch_rope_rotate(const RopeRotateArgs& a);
 int launch_dq_convert_rope(const DqConvertRopeArgs& a);

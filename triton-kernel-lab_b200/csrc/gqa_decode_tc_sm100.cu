@@ -9,8 +9,9 @@
 // run the softmax:
 //
 // * One CTA = (batch, KV head, split), a split being a run of 128-key tiles.
-//   K and V tiles arrive by TMA through three-stage rings (warp 0 K and the
-//   G query rows, warp 2 V), so about 192 KB of the cache is in flight per SM.
+//   K and V tiles arrive by TMA through rings of three stages at head_dim
+//   128 (one CTA per SM) or two at 64 (two CTAs per SM): warp 0 loads K and
+//   the G query rows, warp 2 V; 96-192 KB of the cache in flight per SM.
 // * Scores transposed, S^T = K Q^T: M = 128 keys (TMEM lanes), N = 16 query
 //   heads (G padded with the following rows of q, whose columns are never
 //   read), K = 128 head-dim elements: 8 MMAs into one of two 16-column TMEM
@@ -45,24 +46,40 @@ namespace {
 constexpr int kTcKeys = 128;  // keys per tile (the M of S^T)
 constexpr int kTcD = 128;  // shared-memory layout and O^T rows are sized for head_dim 128
 constexpr int kTcN = 16;  // query heads per MMA (G padded)
-constexpr int kTcStages = 3;
 constexpr int kTcThreads = 256;
-constexpr int kTcTileBytes = kTcKeys * kTcD * 2;  // 32 KB
-constexpr int kTcBlockBytes = kTcKeys * kSwizzleBytes;  // one 64-column block of a tile
-constexpr int kTcQBytes = kTcN * kTcD * 2;  // 4 KB
+constexpr int kTcBlockBytes = kTcKeys * kSwizzleBytes;  // one 64-column block of a K/V tile
 constexpr int kTcQBlockBytes = kTcN * kSwizzleBytes;
 constexpr int kTcPBytes = kTcN * kTcKeys * 2;  // 4 KB
-constexpr int kOffK = 0;
-constexpr int kOffV = kOffK + kTcStages * kTcTileBytes;
-constexpr int kOffQ = kOffV + kTcStages * kTcTileBytes;
-constexpr int kOffP = kOffQ + kTcQBytes;  // two buffers
-constexpr int kOffRed = kOffP + 2 * kTcPBytes;  // float [2][4][16] tile maxima
-constexpr int kOffSum = kOffRed + 2 * 4 * kTcN * 4;  // float [4][16] row sums
-// q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_ready[2], pv_done, o_final
-constexpr int kTcNumBars = 1 + 4 * kTcStages + 2 + 2 + 2;
-constexpr int kOffBar = kOffSum + 4 * kTcN * 4;
-constexpr int kOffCtl = kOffBar + kTcNumBars * 8;
-constexpr int kTcSmemBytes = kOffCtl + 64;
+
+// Shared-memory layout per head_dim.  Barriers first; then the K and V rings
+// (stages of 128 keys x D); then q, P (two buffers) and the reduction
+// scratch.  O^T's second 64-row block reads 16 KB past each V stage (its rows
+// are never read): inside the stage at D = 128 (32 KB stages, the second
+// column block), the next stage or the q/P region at D = 64, which is padded
+// so that the read stays inside the allocation and never touches a barrier.
+// D = 64: two stages, about 81 KB, two CTAs per SM; D = 128: three stages,
+// about 206 KB, one CTA per SM.
+template <int D>
+struct TcCfg {
+  static constexpr int kStages = D == 64 ? 2 : 3;
+  static constexpr int kMinBlocks = D == 64 ? 2 : 1;
+  static constexpr int kTileBytes = kTcKeys * D * 2;
+  static constexpr int kQBytes = kTcN * D * 2;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], p_ready[2], pv_done, o_final
+  static constexpr int kNumBars = 1 + 4 * kStages + 2 + 2 + 2;
+  static constexpr int kOffBar = 0;
+  static constexpr int kOffCtl = kOffBar + kNumBars * 8;
+  static constexpr int kOffK = 1024;
+  static constexpr int kOffV = kOffK + kStages * kTileBytes;
+  static constexpr int kOffQ = kOffV + kStages * kTileBytes;
+  static constexpr int kOffP = kOffQ + ((kQBytes + 1023) / 1024) * 1024;  // two buffers
+  static constexpr int kOffRed = kOffP + 2 * kTcPBytes;  // float [2][4][16] tile maxima
+  static constexpr int kOffSum = kOffRed + 2 * 4 * kTcN * 4;  // float [4][16] row sums
+  static constexpr int kEnd = kOffSum + 4 * kTcN * 4;
+  static constexpr int kPadEnd = kOffV + kStages * kTileBytes + kTcBlockBytes;
+  static constexpr int kSmemBytes = kEnd > kPadEnd ? kEnd : kPadEnd;
+  static_assert(kOffCtl + 64 <= kOffK, "barriers overlap the K ring");
+};
 constexpr uint32_t kColO = 32;  // S^T buffers at columns 0 and 16
 constexpr uint32_t kTcTmemCols = 64;
 constexpr float kTcRescale = 8.0f;
@@ -119,13 +136,14 @@ __device__ __forceinline__ float warp_max_scatter(float (&v)[G], int lane) {
 }
 
 template <int D, int G, bool kBf16>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
     gqa_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                          const __grid_constant__ CUtensorMap tm_v, const int* __restrict__ kv_lens,
                          float* __restrict__ part_o, float* __restrict__ part_ml, int Hkv, int L, int n_splits,
                          int keys_per_split, float scale_log2, unsigned long long timeout_ns, int* status) {
   static_assert(G >= 1 && G <= kTcN, "query heads per KV head must fit one MMA's N");
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  using C = TcCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
     if (threadIdx.x == 0) atomicCAS(status, kOk, kErrMisaligned);
@@ -142,27 +160,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int q_row0 = kv_slab * G;  // query head hkv * G + g of batch b is row b * Hq + hkv * G + g
   const size_t part0 = static_cast<size_t>(q_row0) * n_splits + split;
 
-  uint8_t* sK = smem + kOffK;
-  uint8_t* sV = smem + kOffV;
-  uint8_t* sQ = smem + kOffQ;
-  uint8_t* sP = smem + kOffP;
-  float* sRed = reinterpret_cast<float*>(smem + kOffRed);
-  float* sSum = reinterpret_cast<float*>(smem + kOffSum);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint8_t* sK = smem + C::kOffK;
+  uint8_t* sV = smem + C::kOffV;
+  uint8_t* sQ = smem + C::kOffQ;
+  uint8_t* sP = smem + C::kOffP;
+  float* sRed = reinterpret_cast<float*>(smem + C::kOffRed);
+  float* sSum = reinterpret_cast<float*>(smem + C::kOffSum);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* q_full = bars;
   uint64_t* k_full = q_full + 1;
-  uint64_t* k_empty = k_full + kTcStages;
-  uint64_t* v_full = k_empty + kTcStages;
-  uint64_t* v_empty = v_full + kTcStages;
-  uint64_t* s_full = v_empty + kTcStages;
+  uint64_t* k_empty = k_full + C::kStages;
+  uint64_t* v_full = k_empty + C::kStages;
+  uint64_t* v_empty = v_full + C::kStages;
+  uint64_t* s_full = v_empty + C::kStages;
   uint64_t* p_ready = s_full + 2;
   uint64_t* pv_done = p_ready + 2;
   uint64_t* o_final = pv_done + 1;
-  CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + kOffCtl);
+  CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kOffCtl);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kTcStages; ++i) {
+    for (int i = 0; i < C::kStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
@@ -208,13 +226,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tma_load_3d(sQ + blk * kTcQBlockBytes, &tm_q, q_full, blk * 64, q_row0, 0);
       }
       for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % kTcStages;
-        const uint32_t ph = (j / kTcStages) & 1;
+        const int st = j % C::kStages;
+        const uint32_t ph = (j / C::kStages) & 1;
         if (!mbar_wait(&empty[st], ph ^ 1, ctl, timeout_ns, status, is_k ? 1 : 2)) break;
         mbar_arrive_expect_tx(&full[st], kTcKeys * D * 2);
 #pragma unroll
         for (int blk = 0; blk < D / 64; ++blk)
-          tma_load_3d(ring + st * kTcTileBytes + blk * kTcBlockBytes, map, &full[st], blk * 64,
+          tma_load_3d(ring + st * C::kTileBytes + blk * kTcBlockBytes, map, &full[st], blk * 64,
                       first + j * kTcKeys, kv_slab);
       }
     }
@@ -232,12 +250,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t k_lo0 = sdesc_lo_kmajor(smem_u32(sK));
       const uint32_t v_lo0 = sdesc_lo_mnmajor(smem_u32(sV), kTcKeys);
       const uint32_t p_lo0 = sdesc_lo_kmajor(smem_u32(sP));
-      constexpr uint32_t kStageLo = kTcTileBytes >> 4;
+      constexpr uint32_t kStageLo = C::kTileBytes >> 4;
       constexpr uint32_t kPLo = kTcPBytes >> 4;
       // S^T(j) = K_j Q^T into buffer j & 1.
       auto issue_s = [&](int j) -> bool {
-        const int st = j % kTcStages;
-        if (!warp_wait_tc(&k_full[st], (j / kTcStages) & 1, ctl, timeout_ns, status, 3)) return false;
+        const int st = j % C::kStages;
+        if (!warp_wait_tc(&k_full[st], (j / C::kStages) & 1, ctl, timeout_ns, status, 3)) return false;
         tc_fence_after();
         if (leader) {
 #pragma unroll
@@ -257,8 +275,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // iteration).
         if (j + 1 < n_tiles && !(ok = issue_s(j + 1))) break;
         if (!(ok = warp_wait_tc(&p_ready[j & 1], (j >> 1) & 1, ctl, timeout_ns, status, 5))) break;
-        const int st = j % kTcStages;
-        if (!(ok = warp_wait_tc(&v_full[st], (j / kTcStages) & 1, ctl, timeout_ns, status, 6))) break;
+        const int st = j % C::kStages;
+        if (!(ok = warp_wait_tc(&v_full[st], (j / C::kStages) & 1, ctl, timeout_ns, status, 6))) break;
         tc_fence_after();
         if (leader) {
 #pragma unroll
@@ -413,19 +431,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 template <int D, int G, bool kBf16>
 int launch_tc_t(const GqaDecodeArgs& a, int n_splits, int keys_per_split) {
-  static_assert(kTcSmemBytes <= 232448, "decode shared memory exceeds the sm_100 limit");
+  using C = TcCfg<D>;
+  static_assert(C::kSmemBytes <= 232448, "decode shared memory exceeds the sm_100 limit");
   auto kern = gqa_decode_tc_kernel<D, G, kBf16>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64) return kErrLaunch;
   if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
       return kErrLaunch;
     attr_set[dev] = true;
   }
   dim3 grid(static_cast<unsigned>(n_splits), static_cast<unsigned>(a.Hkv), static_cast<unsigned>(a.B));
-  kern<<<grid, kTcThreads, kTcSmemBytes, a.stream>>>(*a.tm_q, *a.tm_k, *a.tm_v, a.kv_lens, a.part_o, a.part_ml,
+  kern<<<grid, kTcThreads, C::kSmemBytes, a.stream>>>(*a.tm_q, *a.tm_k, *a.tm_v, a.kv_lens, a.part_o, a.part_ml,
                                                      static_cast<int>(a.Hkv), static_cast<int>(a.L), n_splits,
                                                      keys_per_split, a.scale_log2, a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
@@ -445,14 +464,15 @@ int launch_tc_g(const GqaDecodeArgs& a, int n_splits, int keys_per_split) {
 
 bool gqa_decode_tc_supported(int64_t D, int64_t G) { return (D == 64 || D == 128) && (G == 4 || G == 8 || G == 16); }
 
-// Splits per (batch, KV head) for the tensor-core kernel (one CTA per SM):
-// the count that minimises a simple makespan model — waves of CTAs times
-// (128-key tiles per split + a prologue worth about one and a half tiles) —
-// so the last wave is not left mostly empty and short splits do not pay the
-// prologue too often.
-int gqa_decode_splits_tc(int64_t B, int64_t Hkv, int64_t L, int sm_count) {
+// Splits per (batch, KV head) for the tensor-core kernel (one CTA per SM at
+// head_dim 128, two at 64): the count that minimises a simple makespan model
+// — waves of CTAs times (128-key tiles per split + a prologue worth about one
+// and a half tiles) — so the last wave is not left mostly empty and short
+// splits do not pay the prologue too often.
+int gqa_decode_splits_tc(int64_t B, int64_t Hkv, int64_t L, int64_t D, int sm_count) {
   const int64_t tiles = (L + kTcKeys - 1) / kTcKeys;
   const int64_t heads = B * Hkv;
+  sm_count *= D == 64 ? TcCfg<64>::kMinBlocks : TcCfg<128>::kMinBlocks;
   const int64_t cap = tiles < 1024 ? tiles : 1024;
   int64_t best = 1;
   double best_cost = -1.0;
@@ -460,6 +480,9 @@ int gqa_decode_splits_tc(int64_t B, int64_t Hkv, int64_t L, int sm_count) {
     const int64_t per = (tiles + s - 1) / s;
     const int64_t used = (tiles + per - 1) / per;  // splits that hold keys
     if (used != s) continue;
+    // At head_dim 64 a tile is half the bytes, so a one-tile split's fixed
+    // costs (prologue, partials, combine) outweigh what it spreads.
+    if (D == 64 && per < 2 && tiles >= 2) continue;
     const int64_t waves = (heads * s + sm_count - 1) / sm_count;
     const double cost = static_cast<double>(waves) * (static_cast<double>(per) + 1.5);
     if (best_cost < 0.0 || cost < best_cost) {
