@@ -59,6 +59,7 @@ extern "C" {
 #define TK_ERR_DEVICE_TIMEOUT 6 /* low byte; bits 8.. carry the wait site */
 #define TK_ERR_NO_DRIVER 7
 #define TK_ERR_TOO_LARGE 8
+#define TK_ERR_OUT_OF_MEMORY 9 /* device memory the library needs could not be committed */
 
 /* Forward attention.  o receives softmax(scale * q k^T) v (causal: key n
  * attends query m only when n <= m).  lse may be NULL; otherwise it
@@ -105,9 +106,12 @@ TK_API int tk_attn_dq_convert(const float* dq_accum, void* dq, int64_t n, int dt
  * batch*heads*seq*(head_dim+1) <= 16,777,216, else TK_ERR_TOO_LARGE before
  * any launch.  The array is shared by all calls
  * on a device: calls whose kernels overlap on the GPU race on it; each call
- * clears the accumulator it needs.  The first call on a device looks up the
- * array's device address — make it before any stream capture.  Every GPU
- * that loads this part of the library holds the 64 MiB until exit.
+ * clears the accumulator it needs.  Every argument is checked before the
+ * array is touched or anything launches.  The first call on a device looks
+ * up the array's device address — make it before any stream capture; if
+ * the device cannot commit the 64 MiB there (lazy module loading) the call
+ * returns TK_ERR_OUT_OF_MEMORY.  Every GPU that loads this part of the
+ * library holds the 64 MiB until exit.
  * No counterpart in the reference (its backward allocates through torch). */
 TK_API int tk_attn_bwd_noalloc(const void* q, const void* k, const void* v, const void* o,
                                const void* d_o, const float* lse, void* dq, void* dk, void* dv,
@@ -206,17 +210,6 @@ TK_API int tk_attn_set_wait_timeout_ns(unsigned long long timeout_ns);
  * bounded by timeout_ns: exercises the device-timeout path without any
  * fault.  The status word then reads TK_ERR_DEVICE_TIMEOUT. */
 TK_API int tk_attn_selftest_wait_timeout(unsigned long long timeout_ns, void* stream);
-
-/* Diagnostic: one 128 x n x 128 tcgen05 product in the operand form `mode`
- * uses inside the attention kernels, written as fp32 row-major c.
- *   mode 0: c[128][128] = a[128][128] . b[128][128]^T   (both K-major)
- *   mode 1: c[128][n]   = a[128][128] . b[128][n]       (a read from TMEM)
- *   mode 2: c[128][n]   = a[128][128]^T . b[128][n]     (both MN-major)
- *   mode 3: c[128][n]   = a[128][128] . b[128][n]       (a K-major, b MN-major)
- * n is 64 or 128 (ignored for mode 0).  No counterpart in the reference:
- * it pins the operand conventions the kernels rely on. */
-TK_API int tk_attn_diag_umma(const void* a, const void* b, float* c, int mode, int n, int dtype,
-                      void* stream);
 
 /* Human-readable name of a status code. */
 TK_API const char* tk_attn_status_string(int status);

@@ -25,6 +25,37 @@ def pytest_configure(config: pytest.Config) -> None:
     config.addinivalue_line("markers", "gpu: requires a CUDA GPU (B200, sm_100a)")
 
 
+SELFTEST_LIB = ROOT / "triton-kernel-lab_b200" / "tklab" / "_lib" / "libtklab_selftest.so"
+
+
+def load_selftest_lib():
+    """ctypes handle of the test-only probe library (declared in csrc/selftest/tklab_selftest.h)."""
+    import ctypes
+
+    if not SELFTEST_LIB.exists():
+        raise RuntimeError(f"{SELFTEST_LIB.name} is not built: run triton-kernel-lab_b200/build_native.py")
+    lib = ctypes.CDLL(str(SELFTEST_LIB))
+    vp, c_int = ctypes.c_void_p, ctypes.c_int
+    lib.tk_selftest_umma.restype = c_int
+    lib.tk_selftest_umma.argtypes = [vp, vp, vp, c_int, c_int, c_int, vp]
+    lib.tk_selftest_exp2_fma.restype = c_int
+    lib.tk_selftest_exp2_fma.argtypes = [vp, vp, ctypes.c_int64, vp]
+    lib.tk_selftest_status.restype = c_int
+    lib.tk_selftest_status.argtypes = [ctypes.POINTER(c_int), vp]
+    return lib
+
+
+def selftest_status(lib, stream: int) -> int:
+    """Synchronise ``stream`` and read-and-clear the probe library's device status word."""
+    import ctypes
+
+    out = ctypes.c_int(0)
+    rc = lib.tk_selftest_status(ctypes.byref(out), ctypes.c_void_p(stream))
+    if rc != 0:
+        raise RuntimeError(f"tk_selftest_status failed with status {rc}")
+    return int(out.value)
+
+
 def golden_cases(*, rope: bool = False) -> list[str]:
     """Names of the committed golden fixtures: plain attention, or (``rope``) the fused-RoPE cases."""
     names = sorted(path.stem for path in GOLDEN_DIR.glob("*.npz"))

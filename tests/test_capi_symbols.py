@@ -84,3 +84,32 @@ def test_status_strings() -> None:
     assert _native.status_string(6 | (3 << 8)) == "device wait timed out"
     with pytest.raises(RuntimeError, match="wait site 3"):
         _native.check(6 | (3 << 8), "probe")
+
+
+@pytest.mark.parametrize(
+    ("kwargs", "status"),
+    [
+        ({"dq": 0x9008}, 3),
+        ({"q": 0x1004}, 3),
+        ({"lse": 0x6002}, 3),
+        ({"scale": float("nan")}, 1),
+        ({"scale": -1.0}, 1),
+        ({"dtype": 5}, 2),
+        ({"head_dim": 96}, 2),
+        ({"dv": None}, 1),
+        ({"seq": 1 << 20, "heads": 32}, 8),
+    ],
+)
+def test_noalloc_backward_checks_every_argument_before_touching_the_device(kwargs: dict, status: int) -> None:
+    """Refusals come back from host checks alone (no GPU here), so a refused
+    call can never launch work or disturb the shared scratch of a call still
+    running."""
+    args = {"q": 0x1000, "k": 0x2000, "v": 0x3000, "o": 0x4000, "do": 0x5000, "lse": 0x6000, "dq": 0x7000,
+            "dk": 0x8000, "dv": 0x9000, "batch": 1, "heads": 2, "seq": 128, "head_dim": 64, "dtype": 0,
+            "causal": 1, "scale": 0.125, "stream": None}
+    args.update(kwargs)
+    assert _native.load().tk_attn_bwd_noalloc(*args.values()) == status
+
+
+def test_out_of_memory_status_string() -> None:
+    assert _native.status_string(9) == "device memory could not be committed"

@@ -1,8 +1,8 @@
 """GPU: the tcgen05 operand conventions the attention kernels rely on.
 
-``tk_attn_diag_umma`` runs one 128 x n x 128 product per operand form used
-inside the kernels (K-major x K-major, TMEM A x MN-major B, MN-major x
-MN-major, K-major x MN-major).  Each is compared with an fp32 matmul of the
+``tk_selftest_umma`` (in the test-only probe library) runs one 128 x n x 128
+product per operand form used inside the kernels (K-major x K-major, TMEM A
+x MN-major B, MN-major x MN-major, K-major x MN-major).  Each is compared with an fp32 matmul of the
 same 16-bit inputs; the tensor core accumulates in fp32, so agreement is
 tight.
 """
@@ -12,6 +12,7 @@ from __future__ import annotations
 import pytest
 import torch
 
+from conftest import load_selftest_lib, selftest_status
 from tklab import _native
 
 pytestmark = [
@@ -28,13 +29,13 @@ def _run(mode: int, n: int, dtype: torch.dtype) -> tuple[torch.Tensor, torch.Ten
     b_cols = 128 if mode == 0 else n
     b = torch.randn(128, b_cols, generator=gen).to(dtype).cuda()
     c = torch.full((128, b_cols), float("nan"), device="cuda")
-    lib = _native.load()
-    status = lib.tk_attn_diag_umma(
+    lib = load_selftest_lib()
+    status = lib.tk_selftest_umma(
         a.data_ptr(), b.data_ptr(), c.data_ptr(), mode, n, DTYPES[dtype],
         torch.cuda.current_stream().cuda_stream,
     )
-    _native.check(status, "tk_attn_diag_umma")
-    assert _native.device_status(torch.cuda.current_stream().cuda_stream) == 0
+    _native.check(status, "tk_selftest_umma")
+    assert selftest_status(lib, torch.cuda.current_stream().cuda_stream) == 0
     af, bf = a.float(), b.float()
     if mode == 0:
         expected = af @ bf.T

@@ -2,9 +2,12 @@
 
 The library is compiled in-tree with nvcc for ``sm_100a`` only and placed at
 ``tklab/_lib/libtklab_attn.so`` next to the Python package that loads it, so
-it travels with the source tree.  Run ``python build_native.py`` or call
-:func:`build`.  Rebuilds only when a source or header is newer than the
-library unless ``force`` is set.
+it travels with the source tree.  A second, test-only library,
+``tklab/_lib/libtklab_selftest.so`` (``csrc/selftest/``: probes of the
+tcgen05 operand forms and of the FMA-pipe exponential), is built beside it;
+only the tests load it.  Run ``python build_native.py`` or call
+:func:`build`.  Each library is rebuilt only when one of its sources or
+headers is newer than it, unless ``force`` is set.
 """
 
 from __future__ import annotations
@@ -22,6 +25,8 @@ INCLUDE = ROOT.parent / "include"
 BUILD_DIR = ROOT / "_build"
 LIB_DIR = ROOT / "tklab" / "_lib"
 LIB_PATH = LIB_DIR / "libtklab_attn.so"
+SELFTEST_DIR = CSRC / "selftest"
+SELFTEST_LIB_PATH = LIB_DIR / "libtklab_selftest.so"
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CXX_FLAGS = [
@@ -47,20 +52,23 @@ def _nvcc() -> str:
     return nvcc
 
 
-def sources() -> list[Path]:
-    """Return every CUDA translation unit of the library."""
-    return sorted(CSRC.glob("*.cu"))
+def sources(src_dir: Path = CSRC) -> list[Path]:
+    """Return every CUDA translation unit of the library built from ``src_dir``."""
+    return sorted(src_dir.glob("*.cu"))
 
 
-def _deps() -> list[Path]:
-    return sources() + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
+def _deps(src_dir: Path) -> list[Path]:
+    headers = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted(INCLUDE.glob("*.h"))
+    if src_dir != CSRC:
+        headers += sorted(src_dir.glob("*.h"))
+    return sources(src_dir) + headers
 
 
-def _stale() -> bool:
-    if not LIB_PATH.exists():
+def _stale(src_dir: Path, lib_path: Path) -> bool:
+    if not lib_path.exists():
         return True
-    lib_mtime = LIB_PATH.stat().st_mtime
-    return any(dep.stat().st_mtime > lib_mtime for dep in _deps())
+    lib_mtime = lib_path.stat().st_mtime
+    return any(dep.stat().st_mtime > lib_mtime for dep in _deps(src_dir))
 
 
 def _run(cmd: list[str], verbose: bool) -> str:
@@ -72,29 +80,36 @@ def _run(cmd: list[str], verbose: bool) -> str:
     return proc.stdout + proc.stderr
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    """Compile and link the library; return its path."""
-    if not force and not _stale():
-        return LIB_PATH
+def _build_one(src_dir: Path, lib_path: Path, obj_dir: Path, force: bool, verbose: bool, ptxas_info: bool) -> Path:
+    if not force and not _stale(src_dir, lib_path):
+        return lib_path
     nvcc = _nvcc()
-    BUILD_DIR.mkdir(parents=True, exist_ok=True)
+    obj_dir.mkdir(parents=True, exist_ok=True)
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     extra = ["-Xptxas", "-v"] if ptxas_info else []
+    srcs = sources(src_dir)
 
     def compile_one(src: Path) -> tuple[Path, str]:
-        obj = BUILD_DIR / (src.stem + ".o")
+        obj = obj_dir / (src.stem + ".o")
         cmd = [nvcc, *ARCH_FLAGS, *CXX_FLAGS, *extra, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
         return obj, _run(cmd, verbose)
 
-    with ThreadPoolExecutor(max_workers=min(8, len(sources()))) as pool:
-        results = list(pool.map(compile_one, sources()))
+    with ThreadPoolExecutor(max_workers=min(8, len(srcs))) as pool:
+        results = list(pool.map(compile_one, srcs))
     if ptxas_info:
         for _, log in results:
             print(log)
     objs = [str(obj) for obj, _ in results]
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = lib_path.with_suffix(".so.tmp")
     _run([nvcc, *ARCH_FLAGS, "-shared", "-o", str(tmp), *objs], verbose)
-    os.replace(tmp, LIB_PATH)
+    os.replace(tmp, lib_path)
+    return lib_path
+
+
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
+    """Compile and link the attention library and the test-only library; return the former's path."""
+    _build_one(CSRC, LIB_PATH, BUILD_DIR, force, verbose, ptxas_info)
+    _build_one(SELFTEST_DIR, SELFTEST_LIB_PATH, BUILD_DIR / "selftest", force, verbose, ptxas_info)
     return LIB_PATH
 
 

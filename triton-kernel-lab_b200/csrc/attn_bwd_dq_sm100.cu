@@ -387,18 +387,10 @@ int launch_dq_t(const BwdDqArgs& a) {
   using C = DqCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "dQ kernel shared memory exceeds the sm_100 limit");
   auto kern = attn_bwd_dq_kernel<D, kBf16>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    // The setmaxnreg split inside the kernel assumes exactly kDqLaunchRegs
-    // registers per thread at launch; refuse to run a build that differs.
-    cudaFuncAttributes attr;
-    if (cudaFuncGetAttributes(&attr, kern) != cudaSuccess || attr.numRegs != kDqLaunchRegs) return kErrLaunch;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
-      return kErrLaunch;
-    attr_set[dev] = true;
-  }
+  // The setmaxnreg split inside the kernel assumes exactly kDqLaunchRegs
+  // registers per thread at launch; a build that differs is refused.
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, kDqLaunchRegs, nullptr))
+    return rc;
   const int n_tiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
   const long long grid = static_cast<long long>(n_tiles) * a.BH;
   kern<<<static_cast<unsigned>(grid), kDqThreads, C::kSmemBytes, a.stream>>>(

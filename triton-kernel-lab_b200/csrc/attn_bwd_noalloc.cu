@@ -27,7 +27,16 @@
 //     one stream or with events.
 //   * the first call on a device looks up the device address of the array
 //     (cudaGetSymbolAddress, with that device current) and caches it; make
-//     that first call before any stream capture.
+//     that first call before any stream capture.  The 64 MiB are committed
+//     when the library's module is loaded on the device — with lazy module
+//     loading, at that first call — and if the device cannot hold them the
+//     call returns TK_ERR_OUT_OF_MEMORY (the CUDA error is cleared, so later
+//     calls of the library do not see it).
+//   * every argument is checked (pointers, shape, dtype, scale, alignment,
+//     capacity) before the scratch is touched or anything is launched, so a
+//     refused call never disturbs the scratch of an earlier call still
+//     running.
+#include <cmath>
 #include <cstdint>
 #include <mutex>
 
@@ -52,13 +61,18 @@ std::mutex g_scratch_mu;
 // per device, with that device current).
 int scratch_for_current_device(float** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TK_ERR_NO_DRIVER;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return TK_ERR_NO_DRIVER;
+  }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (g_scratch_ptr[dev] == nullptr) {
     float* ptr = nullptr;
-    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch) != cudaSuccess ||
-        ptr == nullptr)
-      return TK_ERR_NO_DRIVER;
+    const cudaError_t err = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();  // clear the sticky-free error so later launches do not report it
+      return err == cudaErrorMemoryAllocation ? TK_ERR_OUT_OF_MEMORY : TK_ERR_NO_DRIVER;
+    }
     g_scratch_ptr[dev] = ptr;
   }
   *out = g_scratch_ptr[dev];
@@ -76,6 +90,12 @@ extern "C" int tk_attn_bwd_noalloc(const void* q, const void* k, const void* v, 
     return TK_ERR_INVALID_ARGUMENT;
   if (batch <= 0 || heads <= 0 || seq <= 0) return TK_ERR_INVALID_ARGUMENT;
   if (head_dim != 64 && head_dim != 128) return TK_ERR_UNSUPPORTED;
+  if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return TK_ERR_UNSUPPORTED;
+  if (!std::isfinite(scale) || scale <= 0.0f) return TK_ERR_INVALID_ARGUMENT;
+  for (const void* p : {q, k, v, o, d_o, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                        static_cast<const void*>(dv)})
+    if (reinterpret_cast<uintptr_t>(p) & 15u) return TK_ERR_MISALIGNED;
+  if (reinterpret_cast<uintptr_t>(lse) & 3u) return TK_ERR_MISALIGNED;
   // Capacity check before anything touches the device.
   const size_t rows = static_cast<size_t>(batch) * static_cast<size_t>(heads) * static_cast<size_t>(seq);
   if (rows > kScratchFloats) return TK_ERR_TOO_LARGE;

@@ -109,9 +109,12 @@ __global__ void wait_timeout_selftest_kernel(unsigned long long timeout_ns, int*
 }
 
 int grid_for(long long work, int threads) {
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();  // a launch on a device that cannot be queried reports its own error
+    sms = 148;
+  }
   long long blocks = (work + threads - 1) / threads;
   const long long cap = static_cast<long long>(sms) * 16;
   if (blocks > cap) blocks = cap;

@@ -6,7 +6,9 @@
 #include <climits>
 #include <cmath>
 #include <cstdint>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "../../include/tklab_attn.h"
 #include "attn_launch.h"
@@ -43,11 +45,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 int status_ptr(int** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return tk::kErrNoDriver;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return tk::kErrNoDriver;
+  }
   std::lock_guard<std::mutex> lock(g_mu);
   if (g_status_ptr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_tk_status_word) != cudaSuccess) return tk::kErrNoDriver;
+    if (cudaGetSymbolAddress(&p, g_tk_status_word) != cudaSuccess) {
+      cudaGetLastError();
+      return tk::kErrNoDriver;
+    }
     g_status_ptr[dev] = static_cast<int*>(p);
   }
   *out = g_status_ptr[dev];
@@ -115,6 +123,40 @@ int make_map_f32(CUtensorMap* map, const float* base, int64_t bh, int64_t seq, i
 constexpr float kLog2e = 1.4426950408889634f;
 
 }  // namespace
+
+namespace tk {
+
+int prepare_kernel(const void* kernel, int smem_bytes, int expect_regs, int* sm_count) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
+    cudaGetLastError();
+    return kErrNoDriver;
+  }
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> prepared;  // (kernel, device) -> SM count
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = prepared.find({kernel, dev});
+  if (it == prepared.end()) {
+    if (expect_regs > 0) {
+      cudaFuncAttributes attr;
+      if (cudaFuncGetAttributes(&attr, kernel) != cudaSuccess || attr.numRegs != expect_regs) {
+        cudaGetLastError();
+        return kErrLaunch;
+      }
+    }
+    int sms = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+      cudaGetLastError();
+      return kErrLaunch;
+    }
+    it = prepared.emplace(std::make_pair(kernel, dev), sms).first;
+  }
+  if (sm_count != nullptr) *sm_count = it->second;
+  return kOk;
+}
+
+}  // namespace tk
 
 extern "C" {
 
@@ -428,24 +470,6 @@ int tk_attn_selftest_wait_timeout(unsigned long long timeout_ns, void* stream) {
   return tk::launch_wait_timeout_selftest(timeout_ns, status, static_cast<cudaStream_t>(stream));
 }
 
-int tk_attn_diag_umma(const void* a, const void* b, float* c, int mode, int n, int dtype,
-                      void* stream) {
-  if (a == nullptr || b == nullptr || c == nullptr) return tk::kErrInvalidArgument;
-  if (mode < 0 || mode > 3) return tk::kErrInvalidArgument;
-  if (mode == 0) n = 128;
-  if (n != 64 && n != 128) return tk::kErrUnsupported;
-  if (dtype != TK_DTYPE_F16 && dtype != TK_DTYPE_BF16) return tk::kErrUnsupported;
-  if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return tk::kErrMisaligned;
-  int* status = nullptr;
-  if (int rc = status_ptr(&status)) return rc;
-  CUtensorMap ma, mb;
-  if (int rc = make_map(&ma, a, 1, 128, 128, dtype)) return rc;
-  if (int rc = make_map(&mb, b, 1, 128, n, dtype)) return rc;
-  return tk::launch_umma_diag(&ma, &mb, static_cast<const uint32_t*>(a), c, mode, n,
-                              dtype == TK_DTYPE_BF16, g_timeout_ns, status,
-                              static_cast<cudaStream_t>(stream));
-}
-
 const char* tk_attn_status_string(int status) {
   switch (status & 0xff) {
     case TK_OK: return "ok";
@@ -457,6 +481,7 @@ const char* tk_attn_status_string(int status) {
     case TK_ERR_DEVICE_TIMEOUT: return "device wait timed out";
     case TK_ERR_NO_DRIVER: return "CUDA driver or device unavailable";
     case TK_ERR_TOO_LARGE: return "problem size exceeds the supported range";
+    case TK_ERR_OUT_OF_MEMORY: return "device memory could not be committed";
     default: return "unknown status";
   }
 }

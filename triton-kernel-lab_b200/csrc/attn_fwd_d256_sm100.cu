@@ -377,25 +377,14 @@ int launch_d256_t(const FwdD256Args& a) {
   using C = WideCfg<NB>;
   static_assert(C::kSmemBytes <= 232448, "wide-head forward shared memory exceeds the sm_100 limit");
   auto kern = attn_fwd_d256_kernel<NB, kBf16>;
-  static bool attr_set[64] = {};
-  static int sm_count[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64) return kErrLaunch;
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
-      return kErrLaunch;
-    if (cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        sm_count[dev] <= 0)
-      return kErrLaunch;
-    attr_set[dev] = true;
-  }
+  int sms = 0;
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, 0, &sms)) return rc;
   const int n_qtiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
   const int units_per_head = a.causal ? (n_qtiles + 1) / 2 : n_qtiles;
   const long long n_units = static_cast<long long>(units_per_head) * a.BH;
   if (n_units > INT32_MAX) return kErrTooLarge;
   // One persistent CTA per SM (shared memory and TMEM allow no second one).
-  const int grid = static_cast<int>(n_units < sm_count[dev] ? n_units : sm_count[dev]);
+  const int grid = static_cast<int>(n_units < sms ? n_units : sms);
   kern<<<grid, kD256Threads, C::kSmemBytes, a.stream>>>(
       *a.tm_q, *a.tm_k, *a.tm_v, static_cast<uint16_t*>(a.o), a.lse, static_cast<int>(a.S), n_qtiles,
       units_per_head, static_cast<int>(n_units), a.causal, static_cast<int>(a.D), a.scale_log2, a.timeout_ns,

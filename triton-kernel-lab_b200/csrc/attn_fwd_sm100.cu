@@ -598,37 +598,23 @@ int launch_fwd_t(const FwdArgs& a) {
   using C = FwdCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "forward shared memory exceeds the sm_100 limit");
   auto kern = attn_fwd_kernel<D, kBf16, kRope>;
-  static bool attr_set[64] = {};
-  static int sm_count[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64) return kErrLaunch;
-  if (!attr_set[dev]) {
-    // The setmaxnreg split inside the kernel assumes exactly kFwdLaunchRegs
-    // registers per thread at launch; refuse to run a build that differs.
-    cudaFuncAttributes attr;
-    if (cudaFuncGetAttributes(&attr, kern) != cudaSuccess || attr.numRegs != kFwdLaunchRegs)
-      return kErrLaunch;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) !=
-        cudaSuccess)
-      return kErrLaunch;
-    if (cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        sm_count[dev] <= 0)
-      return kErrLaunch;
-    attr_set[dev] = true;
-  }
+  // The setmaxnreg split inside the kernel assumes exactly kFwdLaunchRegs
+  // registers per thread at launch; a build that differs is refused.
+  int sms = 0;
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, kFwdLaunchRegs, &sms))
+    return rc;
   const int n_ctiles = static_cast<int>((a.S + 2 * kTileRows - 1) / (2 * kTileRows));
   const long long n_items = static_cast<long long>(n_ctiles) * a.BH;
   const long long n_pair_units = static_cast<long long>((n_ctiles + 1) / 2) * a.BH;
   int mode;
   long long n_units, grid;
-  if (a.causal && n_ctiles > 1 && n_pair_units >= 2LL * sm_count[dev]) {
+  if (a.causal && n_ctiles > 1 && n_pair_units >= 2LL * sms) {
     // Persistent: one CTA per SM walks equal-cost paired units, so the next
     // item's Q load and first products overlap the current epilogue; at
     // least two units per SM keep the last round's imbalance small.
     mode = kOrderPaired;
     n_units = n_pair_units;
-    grid = sm_count[dev];
+    grid = sms;
   } else {
     // One CTA per item, scheduled by the hardware.  Heaviest-first across
     // heads only pays when it cannot thrash L2: K and V of all heads

@@ -170,8 +170,14 @@ int launch_attn_bwd_dkdv(const BwdArgs& a);
 int launch_attn_bwd_dq(const BwdDqArgs& a);
 int launch_attn_dq_convert(const DqConvertArgs& a);
 int launch_wait_timeout_selftest(unsigned long long timeout_ns, int* status, cudaStream_t stream);
-int launch_umma_diag(const CUtensorMap* tm_a, const CUtensorMap* tm_b, const uint32_t* a_words, float* c,
-                     int mode, int n, bool bf16, unsigned long long timeout_ns, int* status,
-                     cudaStream_t stream);
+
+// One-time set-up of a kernel on the current device, guarded by a mutex:
+// checks the registers per thread the kernel was built with against
+// `expect_regs` (when > 0: the setmaxnreg splits inside the kernels assume
+// that exact launch allocation), raises its dynamic shared-memory limit to
+// `smem_bytes`, and caches the device's SM count (returned through
+// `sm_count` when not null).  Errors are cleared from the runtime's
+// last-error slot before returning.
+int prepare_kernel(const void* kernel, int smem_bytes, int expect_regs, int* sm_count);
 
 }  // namespace tk

@@ -434,15 +434,7 @@ int launch_tc_t(const GqaDecodeArgs& a, int n_splits, int keys_per_split) {
   using C = TcCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "decode shared memory exceeds the sm_100 limit");
   auto kern = gqa_decode_tc_kernel<D, G, kBf16>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64) return kErrLaunch;
-  if (!attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes) != cudaSuccess)
-      return kErrLaunch;
-    attr_set[dev] = true;
-  }
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, 0, nullptr)) return rc;
   dim3 grid(static_cast<unsigned>(n_splits), static_cast<unsigned>(a.Hkv), static_cast<unsigned>(a.B));
   kern<<<grid, kTcThreads, C::kSmemBytes, a.stream>>>(*a.tm_q, *a.tm_k, *a.tm_v, a.kv_lens, a.part_o, a.part_ml,
                                                      static_cast<int>(a.Hkv), static_cast<int>(a.L), n_splits,

@@ -1,4 +1,5 @@
-// Diagnostic single-tile tcgen05 GEMM.  It runs one 128 x n x 128 product with
+// Test-only library (libtklab_selftest.so), not part of the attention
+// library: a diagnostic single-tile tcgen05 GEMM.  It runs one 128 x n x 128 product with
 // exactly the operand forms the attention kernels use, so a test can check
 // each convention (descriptor fields, swizzle, TMEM A-operand packing) in
 // isolation against a host matmul:
@@ -6,8 +7,8 @@
 //   mode 1  C = A B     A from TMEM (packed 16-bit), B [128][n] MN-major  (O += P V)
 //   mode 2  C = A^T B   A stored [128 k][128 m] MN-major, B [128][n] MN-major  (dQ = dS K)
 //   mode 3  C = A B     A [128][128] K-major, B [128][n] MN-major    (dK += dS^T Q)
-#include "attn_launch.h"
-#include "sm100_primitives.cuh"
+#include "../sm100_primitives.cuh"
+#include "tklab_selftest_impl.h"
 
 namespace tk {
 namespace {
@@ -121,15 +122,7 @@ __global__ void __launch_bounds__(128, 1)
 int launch_umma_diag(const CUtensorMap* tm_a, const CUtensorMap* tm_b, const uint32_t* a_words, float* c,
                      int mode, int n, bool bf16, unsigned long long timeout_ns, int* status,
                      cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(umma_diag_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDiagSmem) !=
-        cudaSuccess)
-      return kErrLaunch;
-    attr_set[dev] = true;
-  }
+  if (int rc = set_smem_attr_once(reinterpret_cast<const void*>(umma_diag_kernel), kDiagSmem, 0)) return rc;
   umma_diag_kernel<<<1, 128, kDiagSmem, stream>>>(*tm_a, *tm_b, a_words, c, mode, n, bf16 ? 1 : 0,
                                                   timeout_ns, status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;

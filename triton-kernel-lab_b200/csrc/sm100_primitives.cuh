@@ -32,6 +32,7 @@ enum : int {
   kErrDeviceTimeout = 6,
   kErrNoDriver = 7,
   kErrTooLarge = 8,
+  kErrOutOfMemory = 9,
 };
 
 // Bytes of one swizzled column block row (64 16-bit elements).
@@ -464,28 +465,6 @@ __device__ __forceinline__ float lg2(float x) {
   return y;
 }
 
-// Base-2 exponential on the FMA pipe, for splitting a softmax's exponentials
-// between the MUFU (16 per clock per SM) and the FP32 units.  Method
-// (Cody-Waite style range reduction): x = n + f with n = round(x) taken from
-// the low mantissa bits of x + 1.5*2^23, f in [-1/2, 1/2]; 2^f from a degree-4
-// polynomial fitted here for minimum relative error on [-1/2, 1/2]
-// (Lawson-weighted least squares, max relative error 2.7e-6 measured in fp32
-// Horner form); n is added to the exponent field.  Valid for x <= 127;
-// inputs below -126 are clamped to -126, so they return a value of at most
-// 2^-126 instead of 0 (callers use it only where no element is masked).
-__device__ __forceinline__ float exp2_fma(float x) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  x = fmaxf(x, -126.0f);
-  const float t = __fadd_rn(x, kShift);
-  const float n = __fsub_rn(t, kShift);
-  const float f = __fsub_rn(x, n);
-  float p = fmaf(9.570101276e-03f, f, 5.591785908e-02f);
-  p = fmaf(p, f, 2.402474433e-01f);
-  p = fmaf(p, f, 6.931217909e-01f);
-  p = fmaf(p, f, 9.999992847e-01f);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
-}
-
 // ---------------------------------------------------------------------------
 // Packed fp32 pairs (sm_100 fma/add/mul .f32x2: two lanes of fp32 work per
 // issued instruction).  A pair lives in a 64-bit register, `lo` first.
@@ -519,13 +498,18 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
 }
 
 // Two base-2 exponentials on the FMA pipe with packed arithmetic (about five
-// issued instructions per exponential instead of ten).  Same reduction as
-// exp2_fma — n = round(x) from the low mantissa bits of x + 1.5*2^23,
-// f = x - n in [-1/2, 1/2], n added to the exponent field — with a degree-3
+// issued instructions per exponential), for splitting a softmax's
+// exponentials between the MUFU (16 per clock per SM) and the FP32 units.
+// Method (Cody-Waite style range reduction): n = round(x) from the low
+// mantissa bits of x + 1.5*2^23, f = x - n in [-1/2, 1/2], n added to the
+// exponent field of 2^f, which comes from a degree-3
 // polynomial for 2^f fitted here for minimum relative error on [-1/2, 1/2]
 // (Lawson-weighted least squares; max relative error 7.5e-5 in fp32 Horner
-// form, below the 2^-11 rounding of the 16-bit P it feeds).  Inputs below
-// -126 are clamped (result at most 2^-126 instead of 0); valid for x <= 127.
+// form, below the 2^-11 rounding of the 16-bit P it feeds) wherever the
+// result is a normal float (x in [-125.5, 127]); in [-126, -125.5) a result
+// just below 2^-126 comes out subnormal, relative error up to 1.5e-4.
+// Inputs below -126 are clamped (result in [0, 2^-126] instead of 0); valid
+// for x <= 127.  tests/test_exp2_fma.py checks these bounds.
 __device__ __forceinline__ void exp2_fma_pair(float x0, float x1, float& p0, float& p1) {
   constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
   const uint64_t x = f2_pack(fmaxf(x0, -126.0f), fmaxf(x1, -126.0f));

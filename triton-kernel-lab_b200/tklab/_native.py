@@ -93,7 +93,6 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "tk_attn_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), _vp]),
     "tk_attn_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_ulonglong]),
     "tk_attn_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_ulonglong, _vp]),
-    "tk_attn_diag_umma": (ctypes.c_int, [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp]),
     "tk_attn_status_string": (ctypes.c_char_p, [ctypes.c_int]),
 }
 
