@@ -166,6 +166,30 @@ def _make_inputs(shape: tuple[int, ...], dtype: torch.dtype, qk_std: float, seed
     return [q, k, v, do]
 
 
+def _metric_and_config(config: str, world: int, bh_total: int | None = None) -> tuple[str, dict]:
+    """The metric name and the ``config`` object of a run of ``config`` on ``world`` GPUs.
+
+    Both arms (ours and ``--impl reference``) print exactly these, so the two
+    lines describe the same workload."""
+    b, h, s, d, dtype, causal, _ = CONFIGS[config]
+    bh_total = b * h if bh_total is None else bh_total
+    dtype_name = "bf16" if dtype == torch.bfloat16 else "fp16"
+    metric = (f"attention fwd+bwd TFLOP/s ({'causal' if causal else 'non-causal'} {dtype_name} "
+              f"B={b} H={h} S={s} D={d}), aggregate over GPUs")
+    per_rank = -(-bh_total // world)
+    cfg = {
+        "workload": f"{config}: causal={causal} B={b} H={h} S={s} D={d} {str(dtype).split('.')[-1]}",
+        "global_batch": b,
+        "seq_len": s,
+        "heads": h,
+        "head_dim": d,
+        "parallelism": f"(batch*head) slabs {per_rank}/rank x {world} ranks, no collective",
+        "bh_total": bh_total,
+        "l2": "flushed: 256 MiB write before every timed step (outside its events)",
+    }
+    return metric, cfg
+
+
 def run_ours(args: argparse.Namespace) -> None:
     from tklab import _native
     from tklab.kernels.flash_attention import _NATIVE_DTYPE, attention_causal, attention_noncausal
@@ -222,12 +246,16 @@ def run_ours(args: argparse.Namespace) -> None:
         _native.check(lib.tk_attn_dq_convert(dq_accum.data_ptr(), dq.data_ptr(), numel, nd, sp), "dq_convert")
         mark(4)
 
-    # The clock sampler runs from before the warm-up so that its samples
-    # cover the whole timed region, however short.
-    sampler = ClockSampler(local_rank) if rank == 0 else None
-    if sampler:
-        sampler.__enter__()
-        sampler.wait_first()
+    # Every rank samples its own GPU's clocks, from before the warm-up so
+    # that the samples cover the whole timed region, however short.
+    sampler = ClockSampler(local_rank)
+    sampler.__enter__()
+    sampler.wait_first()
+    liveness = None
+    if world > 1:
+        from tklab.sharding import check_ranks_alive, liveness_group
+
+        liveness = liveness_group()
     try:
         for _ in range(args.warmup):
             flush.zero_()
@@ -239,6 +267,9 @@ def run_ours(args: argparse.Namespace) -> None:
 
         events = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
         if world > 1:
+            # Between warm-up and timing, with nothing in flight: a rank that
+            # has gone is reported here instead of blocking the barrier.
+            check_ranks_alive(liveness, timeout_s=60.0)
             torch.distributed.barrier()
         torch.cuda.synchronize(device)
         t_start = time.monotonic()
@@ -247,11 +278,9 @@ def run_ours(args: argparse.Namespace) -> None:
             step(events[i])
         torch.cuda.synchronize(device)
         t_end = time.monotonic()
-        if sampler:
-            time.sleep(2 * sampler.interval_ms / 1000.0)
+        time.sleep(2 * sampler.interval_ms / 1000.0)
     finally:
-        if sampler:
-            sampler.__exit__()
+        sampler.__exit__()
     if world > 1:
         torch.distributed.barrier()
     status = _native.device_status(sp)
@@ -264,10 +293,34 @@ def run_ours(args: argparse.Namespace) -> None:
         for j in range(4):
             per_kernel[j] += ev[j].elapsed_time(ev[j + 1])
         total_ms += ev[0].elapsed_time(ev[4])
-    times = torch.tensor([total_ms] + per_kernel, dtype=torch.float64, device=device)
+    my_clocks = sampler.summary(t_start, t_end)
+    reason_mask = sum(bit for bit, name in THROTTLE_REASONS.items() if name in my_clocks["reasons"])
+    mine = [total_ms] + per_kernel + [my_clocks["sm_mhz"] or 0.0, my_clocks["sm_max_mhz"] or 0.0,
+                                      float(reason_mask), float(my_clocks["samples"])]
     if world > 1:
-        torch.distributed.all_reduce(times, op=torch.distributed.ReduceOp.MAX)
-    total_ms, k_fwd, k_pre, k_bwd, k_cvt = times.tolist()
+        gathered = [torch.zeros(len(mine), dtype=torch.float64, device=device) for _ in range(world)]
+        torch.distributed.all_gather(gathered, torch.tensor(mine, dtype=torch.float64, device=device))
+        rows = [g.tolist() for g in gathered]
+    else:
+        rows = [mine]
+    # Whole-job time = the slowest rank's (max over ranks, per column).
+    total_ms, k_fwd, k_pre, k_bwd, k_cvt = (max(r[j] for r in rows) for j in range(5))
+    per_rank = [
+        {
+            "rank": i,
+            "ms_per_step": round(r[0] / args.steps, 4),
+            "kernel_ms_per_step": {name: round(r[1 + j] / args.steps, 4)
+                                   for j, name in enumerate(("attn_fwd", "attn_bwd_pre", "attn_bwd_fused",
+                                                             "dq_convert"))},
+            "sm_mhz": r[5] or None,
+            "sm_max_mhz": r[6] or None,
+            "reasons": [name for bit, name in THROTTLE_REASONS.items() if int(r[7]) & bit],
+            "clock_samples": int(r[8]),
+            # time x clock: comparable across ranks whose clocks differ
+            "ms_x_ghz": round(r[0] / args.steps * (r[5] or 0.0) / 1000.0, 4),
+        }
+        for i, r in enumerate(rows)
+    ]
 
     # End-to-end through the public autograd API with host buffers.
     e2e = None
@@ -292,9 +345,12 @@ def run_ours(args: argparse.Namespace) -> None:
         dom = max(kernels, key=lambda n: kernels[n][0])
         dom_ms, dom_flops = kernels[dom]
         achieved = dom_flops / (dom_ms * 1e-3) / 1e12
-        clocks = sampler.summary(t_start, t_end) if sampler else None
+        clocks = dict(my_clocks)
+        clocks["reasons"] = sorted({name for r in per_rank for name in r["reasons"]})
+        clocks["sm_mhz_min_over_ranks"] = min((r["sm_mhz"] or 0.0) for r in per_rank)
+        metric, config = _metric_and_config(args.config, world, bh_total)
         line = {
-            "metric": "attention fwd+bwd TFLOP/s (causal bf16 B=8 H=32 S=4096 D=128), aggregate over GPUs",
+            "metric": metric,
             "value": round(value, 2),
             "unit": "TFLOP/s",
             "n_gpus": world,
@@ -306,16 +362,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "vs_baseline": None,
             "dtype": "bf16" if dtype == torch.bfloat16 else "f16",
             "data": "synthetic (seeded randn; Q,K std %.1f)" % qk_std,
-            "config": {
-                "workload": f"{args.config}: causal={causal} B={b} H={h} S={s} D={d} {str(dtype).split('.')[-1]}",
-                "global_batch": b,
-                "seq_len": s,
-                "heads": h,
-                "head_dim": d,
-                "parallelism": f"(batch*head) slabs {slab}/rank x {world} ranks, no collective",
-                "bh_total": bh_total,
-                "l2": "flushed: 256 MiB write before every timed step (outside its events)",
-            },
+            "config": config,
             "fwd_tflops_per_gpu": round(ff / world / (k_fwd / steps * 1e-3) / 1e12, 2),
             "bwd_tflops_per_gpu": round(bf / world / ((k_pre + k_bwd + k_cvt) / steps * 1e-3) / 1e12, 2),
             "pct_peak_fwd": round(100 * ff / world / (k_fwd / steps * 1e-3) / 1e12 / peaks["bf16_tflops"], 2),
@@ -340,6 +387,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "gpu_launches": 4 * steps,
             "gpu_launches_note": "per rank: fwd, bwd_pre, bwd_fused, dq_convert per step",
             "clocks": clocks,
+            "per_rank": per_rank,
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
@@ -474,9 +522,10 @@ def run_reference(args: argparse.Namespace) -> None:
     per_step = total / args.steps
     flops = fwd_flops(1, 1, s, d, causal) + bwd_flops(1, 1, s, d, causal)
     value = flops / per_step / 1e12
+    metric, config = _metric_and_config(args.config, world)
     line = {
         "impl": "reference",
-        "metric": "attention fwd+bwd TFLOP/s (causal bf16 B=8 H=32 S=4096 D=128), aggregate over GPUs",
+        "metric": metric,
         "value": round(value, 4),
         "unit": "TFLOP/s",
         "n_gpus": world,
@@ -488,11 +537,11 @@ def run_reference(args: argparse.Namespace) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded randn)",
-        "config": {"workload": f"{args.config}: one (b,h) slab per step of B={b} H={h} S={s} D={d}",
-                   "global_batch": b, "seq_len": s},
+        "config": config,
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                          "kind": "reference",
-                         "sample": f"one (b,h) slab ({s}x{d}) fp32 SDPA fwd+autograd bwd per step"},
+                         "sample": f"one (b,h) slab ({s}x{d}) of the workload per step: fp32 SDPA fwd + "
+                                   "autograd bwd on the host cores"},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

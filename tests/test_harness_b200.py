@@ -17,7 +17,9 @@ import pytest
 import torch
 
 import tklab.kernels  # noqa: F401  (registers the attention specs)
+from tklab import cli
 from tklab.harness import attention_memory, bench, results, roofline
+from tklab.harness.jsonio import write_json_atomic
 from tklab.registry import REGISTRY
 
 MEASURED = {
@@ -104,13 +106,16 @@ def test_peaks_from_measurement() -> None:
         )
 
 
-@pytest.mark.skipif(not roofline.DEFAULT_MEASURED_PEAKS.exists(), reason="no MEASURED_PEAKS.json in this checkout")
-def test_measured_peaks_file_is_readable() -> None:
-    data = json.loads(roofline.DEFAULT_MEASURED_PEAKS.read_text())
-    peaks = roofline.peaks_from_measurement(
-        data, gpu_name=data["gpu_name"], compute_capability="10.0", torch_version="t", source="file"
-    )
-    assert peaks["peak_bw_gbps"] > 1000 and peaks["cublas_tflops_fp16_fp32acc"] > 500
+def test_b200_profile_is_sourced() -> None:
+    """Theoretical ceilings come only from a profile with primary-source URLs (reference docs/benchmarking.md:60-62)."""
+    for profile in (roofline.B200_PROFILE, roofline.RTX4060_PROFILE):
+        assert profile.product_spec_url.startswith("https://www.nvidia.com/")
+        assert profile.architecture_whitepaper_url.startswith("https://")
+
+
+def test_peaks_file_is_named_explicitly_never_found_in_the_checkout() -> None:
+    assert not hasattr(roofline, "DEFAULT_MEASURED_PEAKS")
+    assert roofline.MEASURED_PEAKS_ENV == "TKLAB_MEASURED_PEAKS"
 
 
 def test_roofline_point() -> None:
@@ -177,7 +182,7 @@ def test_results_table_only_reads_existing_files(tmp_path: Path, capsys: pytest.
         payload = results.result_payload(
             spec, rows=[_row(2048, 0.05)], peaks=_peaks(), benchmark_started_at_utc="now", benchmark_preflight_gpu_utilization_pct=()
         )
-        results.write_json_atomic(tmp_path / "nvidia_b200" / f"{name}.json", payload)
+        write_json_atomic(tmp_path / "nvidia_b200" / f"{name}.json", payload)
     assert results.main(["--table-only", "--results-dir", str(tmp_path), "--title", "B200 roofline"]) == 0
     out = capsys.readouterr().out
     assert "B200 roofline" in out and "flash_attn causal float16" in out and "% ceiling" in out
@@ -257,17 +262,42 @@ def test_bench_spec_rows_on_b200() -> None:
     assert row["block_m"] == 128 and row["causal"] is True
 
 
+def _peaks_file() -> Path | None:
+    """The driver-measured peaks of this pool when the checkout carries them (else a live measurement)."""
+    path = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    return path if path.exists() else None
+
+
 @pytest.mark.gpu
 @gpu
-def test_results_run_writes_schema7_file(tmp_path: Path) -> None:
-    paths = results.run(
-        ["attention_noncausal"], results_dir=tmp_path, warmup_ms=5, repetition_ms=20, sizes=(1024,), allow_busy_gpu=True
+def test_cli_run_benchmarks_writes_schema7_file(tmp_path: Path) -> None:
+    options = cli.BenchmarkOptions(
+        device=0, force_peaks=False, kernels=("attention_noncausal",), warmup_ms=5, repetition_ms=20,
+        list_kernels=False, allow_busy_gpu=True, results_dir=tmp_path, peaks=_peaks_file(), sizes=(1024,),
     )
-    payload = json.loads(paths["attention_noncausal"].read_text())
+    payloads = cli.run_benchmarks(options)
+    path = payloads["attention_noncausal"]["path"]
+    payload = json.loads(path.read_text())
     assert [key for key in payload if key != "peaks_source"] == REFERENCE_RESULT_KEYS
     assert payload["gpu"] == torch.cuda.get_device_name(0)
     assert {row["dtype"] for row in payload["rows"]} == {"float16", "bfloat16"}
-    assert paths["attention_noncausal"].parent.name == roofline.gpu_slug(0)
+    assert path.parent.name == roofline.gpu_slug(0)
+    assert (path.parent / "peaks.json").exists()
+
+
+@pytest.mark.gpu
+@gpu
+def test_cli_main_as_the_reference_benchmark_script_calls_it(tmp_path: Path) -> None:
+    """``benchmarks/run.py`` of the reference is ``raise SystemExit(main())`` over ``tklab.cli.main``."""
+    argv = ["--kernel", "attention_causal", "--size", "512", "--warmup-ms", "5", "--repetition-ms", "20",
+            "--allow-busy-gpu", "--results-dir", str(tmp_path)]
+    peaks = _peaks_file()
+    if peaks is not None:
+        argv += ["--peaks", str(peaks)]
+    assert cli.main(argv) == 0
+    payload = json.loads((tmp_path / roofline.gpu_slug(0) / "attention_causal.json").read_text())
+    assert payload["schema_version"] == 7 and payload["kernel"] == "attention_causal"
+    assert all(row["size"] == 512 and row["tflops"] > 0 for row in payload["rows"])
 
 
 @pytest.mark.gpu
@@ -286,3 +316,54 @@ def test_flash_attention_memory_is_linear() -> None:
     dense_slope = attention_memory.empirical_slope([dense_small, dense_large])
     assert dense_slope is not None and dense_slope > 1.8
     assert math.isfinite(dense_slope)
+
+
+def test_cli_options_mirror_the_reference() -> None:
+    options = cli.parse_args([])
+    assert options == cli.BenchmarkOptions(
+        device=0, force_peaks=False, kernels=None, warmup_ms=25, repetition_ms=100, list_kernels=False,
+        allow_busy_gpu=False,
+    )
+    chosen = cli.parse_args(["--kernel", "attention_causal", "--kernel", "attention_noncausal", "--device", "1"])
+    assert chosen.kernels == ("attention_causal", "attention_noncausal") and chosen.device == 1
+    with pytest.raises(SystemExit):
+        cli.parse_args(["--kernel", "matmul_fp32acc"])
+    with pytest.raises(ValueError, match="no kernels selected"):
+        cli._select_specs(("not-registered",))
+    assert [spec.name for spec in cli._select_specs(("attention_causal", "attention_noncausal"))] == [
+        name for name in REGISTRY if name in ("attention_causal", "attention_noncausal")
+    ]
+
+
+def test_cli_list_kernels(capsys: pytest.CaptureFixture[str]) -> None:
+    assert cli.main(["--list-kernels"]) == 0
+    out = capsys.readouterr().out
+    assert "attention_causal:" in out and "attention_noncausal:" in out
+
+
+def test_cli_requires_cuda_before_anything_else(monkeypatch: pytest.MonkeyPatch) -> None:
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)
+    with pytest.raises(RuntimeError, match="CUDA is required for benchmarks"):
+        cli.run_benchmarks(cli.parse_args([]))
+
+
+REFERENCE_RUN_PY = Path("/root/reference/benchmarks/run.py")
+
+
+@pytest.mark.skipif(not REFERENCE_RUN_PY.exists(), reason="the reference checkout is not present on this machine")
+def test_reference_benchmark_script_runs_unchanged_on_this_package() -> None:
+    """The reference's own ``benchmarks/run.py`` (``from tklab.cli import main``), unmodified, on this package."""
+    import subprocess
+    import sys
+
+    package_dir = Path(__file__).resolve().parents[1] / "triton-kernel-lab_b200"
+    proc = subprocess.run(
+        [sys.executable, str(REFERENCE_RUN_PY), "--list-kernels"],
+        env={"PYTHONPATH": str(package_dir), "PATH": "/usr/bin:/bin"},
+        capture_output=True,
+        text=True,
+        timeout=300,
+        check=False,
+    )
+    assert proc.returncode == 0, proc.stderr
+    assert "attention_causal:" in proc.stdout and "attention_noncausal:" in proc.stdout

@@ -1,8 +1,11 @@
-"""CPU: the multi-rank host logic of the sharded attention path (gloo, world_size 2).
+"""CPU: the multi-rank host logic of the sharded attention path (gloo).
 
 Each rank takes its (batch*head) slab, computes attention on it (the CPU
 oracle stands in for the kernels here), and the gathered slabs must equal
-the unsharded result; the timing reduction is the MAX over ranks.
+the unsharded result; the timing reduction is the MAX over ranks.  A
+failure test makes one rank leave between steps (it exits without another
+collective) and checks that the survivors' liveness check names it within a
+bounded time and that the parent sees every process end.
 """
 
 from __future__ import annotations
@@ -10,6 +13,8 @@ from __future__ import annotations
 import os
 import socket
 import sys
+import time
+from datetime import timedelta
 from pathlib import Path
 
 import pytest
@@ -17,7 +22,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from tklab.sharding import slab_range, slab_view
+from tklab.sharding import check_ranks_alive, slab_range, slab_view
 
 
 def test_slab_ranges_tile_the_axis() -> None:
@@ -77,3 +82,69 @@ def test_two_rank_gloo_shards_match_unsharded() -> None:
         mp.start_processes(_worker, args=(2, _free_port(), root, out), nprocs=2, start_method="spawn")
         assert out["max_err"] == 0.0
         assert out["t_max"] == 2.0
+
+
+def _leaving_worker(rank: int, world: int, port: int, root: str, leaver: int, out: dict) -> None:
+    sys.path[:0] = [str(Path(root) / "triton-kernel-lab_b200"), root]
+    from tklab.sharding import check_ranks_alive as alive
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    # Step 1: everybody present.
+    alive(timeout_s=5.0)
+    t = torch.tensor([float(rank)])
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    if rank == leaver:
+        out[f"left{rank}"] = True
+        os._exit(0)  # leaves between steps: nothing of this rank in flight
+    # Step 2: the survivors must learn of the departure before launching anything.
+    start = time.monotonic()
+    try:
+        alive(timeout_s=2.0)
+        out[f"rank{rank}"] = "no error"
+    except RuntimeError as error:
+        out[f"rank{rank}"] = str(error)
+    out[f"seconds{rank}"] = time.monotonic() - start
+    os._exit(0)
+
+
+def test_a_rank_that_leaves_between_steps_is_reported_not_waited_for() -> None:
+    root = str(Path(__file__).resolve().parents[1])
+    world, leaver = 3, 2
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        out = manager.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_leaving_worker, args=(rank, world, port, root, leaver, out)) for rank in range(world)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        alive_procs = [p for p in procs if p.is_alive()]
+        for p in alive_procs:
+            p.kill()
+        assert not alive_procs, "a survivor blocked instead of reporting the missing rank"
+        assert out.get(f"left{leaver}") is True
+        assert "2" in out["rank0"] and "liveness check failed on rank 0" in out["rank0"], out["rank0"]
+        assert out["rank1"].startswith("rank liveness check failed on rank 1"), out["rank1"]
+        assert out["seconds0"] < 30 and out["seconds1"] < 30
+
+
+def test_liveness_check_passes_with_every_rank_present() -> None:
+    root = str(Path(__file__).resolve().parents[1])
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        out = manager.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_leaving_worker, args=(rank, 2, port, root, -1, out)) for rank in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        assert all(not p.is_alive() for p in procs)
+        assert out["rank0"] == "no error" and out["rank1"] == "no error"
+
+
+def test_liveness_timeout_must_be_positive() -> None:
+    with pytest.raises(ValueError):
+        check_ranks_alive(timeout_s=0)

@@ -1,37 +1,32 @@
-"""Schema-7 benchmark result files and the attention roofline point on B200.
+"""Schema-7 benchmark result files and the attention roofline table on B200.
 
-``python -m tklab.harness.results [--kernel NAME]... [--results-dir DIR]``
-benchmarks the registered attention kernels with
-:func:`tklab.harness.bench.bench_spec` and writes one
-``<results-dir>/<gpu-slug>/<kernel>.json`` per kernel in the reference's
-schema-7 layout (``src/tklab/cli.py:114-183`` ``run_benchmarks`` and
-``:253-291`` ``_result_payload``), with the ceilings from
-``MEASURED_PEAKS.json`` (:func:`tklab.harness.roofline.load_measured_peaks`).
+The result payload (``result_payload``) and the baseline choice
+(``compute_baselines``) are the reference's ``src/tklab/cli.py:253-291`` and
+``:234-250``; ``tklab.cli`` (the reference's ``tklab-bench`` entry point)
+writes the files with them.
 
-It then prints the table the reference's ``benchmarks/plot_roofline.py``
-prints under its figure (``:296-299``: kernel, throughput, percent of
-ceiling, analytic intensity) for the flash-attention points, with the
-results directory and the title taken from options instead of the
-hard-coded RTX 4060 ones (``:30``, ``:290``).  The PNG itself needs
-matplotlib, which this environment does not have; the JSON and the table
-carry the same numbers.
+``python -m tklab.harness.results [--kernel NAME]... [--results-dir DIR]
+[--title TITLE] [--table-only]`` runs that benchmark (unless
+``--table-only``) and prints the table the reference's
+``benchmarks/plot_roofline.py`` prints under its figure (``:296-299``:
+kernel, throughput, percent of ceiling, analytic intensity) for the
+flash-attention points, with the results directory and the title taken
+from options instead of the hard-coded RTX 4060 ones (``:30``, ``:290``).
+The PNG itself needs matplotlib, which this environment does not have; the
+JSON and the table carry the same numbers.
 """
 
 from __future__ import annotations
 
 import argparse
-import time
 from collections.abc import Sequence
-from datetime import datetime, timezone
 from pathlib import Path
 from typing import Any, cast
 
-import torch
-
 import tklab.kernels  # noqa: F401  (registers the attention specs)
-from tklab.harness.bench import BenchRow, bench_spec
-from tklab.harness.jsonio import JsonObject, read_json_object, write_json_atomic
-from tklab.harness.roofline import PeakResults, gpu_utilization_pct, load_measured_peaks, roofline_point
+from tklab.harness.bench import BenchRow
+from tklab.harness.jsonio import JsonObject, read_json_object
+from tklab.harness.roofline import PeakResults, roofline_point
 from tklab.registry import REGISTRY, KernelSpec
 
 RESULT_SCHEMA_VERSION = 7
@@ -137,76 +132,6 @@ def print_roofline_table(points: Sequence[dict[str, Any]], *, title: str) -> Non
         )
 
 
-def _utilization_samples(device: int, count: int = 5, interval_s: float = 1.0) -> tuple[int, ...]:
-    """Whole-device utilization sampled before benchmarking (``cli.py:215-231``)."""
-    samples = []
-    for index in range(count):
-        samples.append(gpu_utilization_pct(device))
-        if index + 1 < count:
-            time.sleep(interval_s)
-    return tuple(samples)
-
-
-def run(
-    kernels: Sequence[str],
-    *,
-    results_dir: Path,
-    device: int = 0,
-    warmup_ms: int = 25,
-    repetition_ms: int = 100,
-    sizes: Sequence[int] | None = None,
-    allow_busy_gpu: bool = False,
-    peaks_path: Path | None = None,
-) -> dict[str, Path]:
-    """Benchmark ``kernels`` and write their result files; returns name -> path.
-
-    Raises:
-        RuntimeError: If CUDA is unavailable or the GPU is busy (unless allowed).
-        ValueError: If a kernel name is not registered.
-    """
-    if not torch.cuda.is_available():
-        raise RuntimeError("CUDA is required for benchmarks")
-    unknown = sorted(set(kernels) - set(REGISTRY))
-    if unknown:
-        raise ValueError(f"unknown kernel(s): {', '.join(unknown)}")
-    started = datetime.now(timezone.utc).isoformat()
-    utilization = _utilization_samples(device)
-    if not allow_busy_gpu and max(utilization) > MAX_IDLE_GPU_UTILIZATION_PCT:
-        raise RuntimeError(
-            f"GPU {device} reached {max(utilization)}% utilization during preflight; "
-            "close GPU workloads or pass --allow-busy-gpu to accept contaminated results"
-        )
-    peaks = load_measured_peaks(peaks_path, device=device)
-    out_dir = results_dir / peaks["gpu_slug"]
-    written: dict[str, Path] = {}
-    for name in kernels:
-        spec = REGISTRY[name]
-        cublas_tflops, theoretical_tflops = compute_baselines(spec, peaks)
-        rows = bench_spec(
-            spec,
-            peak_bw_gbps=peaks["peak_bw_gbps"],
-            cublas_tflops=cublas_tflops,
-            theoretical_tflops=theoretical_tflops,
-            device=device,
-            warmup_ms=warmup_ms,
-            repetition_ms=repetition_ms,
-            sizes=sizes,
-        )
-        path = out_dir / f"{name}.json"
-        write_json_atomic(
-            path,
-            result_payload(
-                spec,
-                rows=rows,
-                peaks=peaks,
-                benchmark_started_at_utc=started,
-                benchmark_preflight_gpu_utilization_pct=utilization,
-            ),
-        )
-        written[name] = path
-    return written
-
-
 def main(argv: Sequence[str] | None = None) -> int:
     """Command-line entry point."""
     parser = argparse.ArgumentParser(prog="python -m tklab.harness.results", description=__doc__.split("\n")[0])
@@ -218,7 +143,7 @@ def main(argv: Sequence[str] | None = None) -> int:
     parser.add_argument("--warmup-ms", type=int, default=25)
     parser.add_argument("--repetition-ms", type=int, default=100)
     parser.add_argument("--allow-busy-gpu", action="store_true")
-    parser.add_argument("--peaks", type=Path, default=None, help="MEASURED_PEAKS.json to use")
+    parser.add_argument("--peaks", type=Path, default=None, help="peak-measurement JSON to take the ceilings from")
     parser.add_argument("--table-only", action="store_true", help="print the table from existing result files")
     options = parser.parse_args(argv)
     kernels = options.kernels or ["attention_noncausal", "attention_causal"]
@@ -230,16 +155,23 @@ def main(argv: Sequence[str] | None = None) -> int:
                 raise FileNotFoundError(f"no result file for {name} under {options.results_dir}")
             paths[name] = matches[-1]
     else:
-        paths = run(
-            kernels,
-            results_dir=options.results_dir,
-            device=options.device,
-            warmup_ms=options.warmup_ms,
-            repetition_ms=options.repetition_ms,
-            sizes=options.sizes,
-            allow_busy_gpu=options.allow_busy_gpu,
-            peaks_path=options.peaks,
+        from tklab.cli import BenchmarkOptions, run_benchmarks
+
+        payloads = run_benchmarks(
+            BenchmarkOptions(
+                device=options.device,
+                force_peaks=False,
+                kernels=tuple(kernels),
+                warmup_ms=options.warmup_ms,
+                repetition_ms=options.repetition_ms,
+                list_kernels=False,
+                allow_busy_gpu=options.allow_busy_gpu,
+                results_dir=options.results_dir,
+                peaks=options.peaks,
+                sizes=tuple(options.sizes) if options.sizes else None,
+            )
         )
+        paths = {name: payload["path"] for name, payload in payloads.items()}
     points: list[dict[str, Any]] = []
     gpu = ""
     for name, path in paths.items():

@@ -10,27 +10,33 @@ the attention benchmark rows and the roofline figure consume:
   FP32-accumulate one, which is a GeForce property; data-center Blackwell
   runs both at the same rate, so the profile carries that ratio.
 * The schema-7 peak payload (``PeakResults``, ``:110-144``) that result files
-  embed.  On B200 the empirical ceilings are not re-measured here: they
-  come from ``MEASURED_PEAKS.json`` at the repository root, a device-copy
-  bandwidth and a cuBLAS bf16 GEMM rate measured on the same machines
-  (fp16 and bf16 run at the same tensor-core rate on sm_100).
+  embed, and :func:`load_or_measure_peaks` (``:354-405``): a compatible
+  ``<results>/<gpu-slug>/peaks.json`` is reused; otherwise the ceilings come
+  from a measurement file named explicitly (argument, or the
+  ``TKLAB_MEASURED_PEAKS`` environment variable: a device-copy bandwidth and
+  a cuBLAS bf16 GEMM rate measured on the same machines) or are measured
+  live (:func:`measure_peaks`), then written to ``peaks.json``.
 """
 
 from __future__ import annotations
 
+import os
 import re
 import subprocess
+import threading
+import time
 from collections.abc import Mapping
 from dataclasses import dataclass
+from datetime import datetime, timezone
 from pathlib import Path
-from typing import Any, TypedDict
+from typing import Any, TypedDict, cast
 
 import torch
 
-from tklab.harness.jsonio import read_json_object
+from tklab.harness.jsonio import JsonObject, read_json_object, write_json_atomic
 
 PEAKS_SCHEMA_VERSION = 7
-DEFAULT_MEASURED_PEAKS = Path(__file__).resolve().parents[3] / "MEASURED_PEAKS.json"
+MEASURED_PEAKS_ENV = "TKLAB_MEASURED_PEAKS"
 
 
 @dataclass(frozen=True, slots=True)
@@ -84,17 +90,17 @@ RTX4060_PROFILE = GpuTheoreticalProfile(
 # fp32 accumulation, i.e. 8,192 FLOP per clock per SM, 2,048 per tensor
 # core; fp16 accumulation does not go faster.  1,965 MHz is the part's
 # `clocks.max.sm`.  At that clock the ceiling is 2,383 TFLOP/s, against
-# NVIDIA's 2.25 PFLOP/s dense figure at the HGX power limit.
+# NVIDIA's 2.25 PFLOP/s dense FP16/BF16 figure per GPU (the HGX B200
+# product page, 36 PFLOP/s per 8 GPUs with sparsity); the SM count and the
+# tensor-core generation are in the Blackwell architecture technical brief.
 B200_PROFILE = GpuTheoreticalProfile(
     model_substring="B200",
     rated_boost_mhz=1965,
     streaming_multiprocessors=148,
     tensor_cores_per_sm=4,
     fp16_fp32acc_flops_per_clock_per_tensor_core=2048,
-    product_spec_url="measured: nvidia-smi clocks.max.sm = 1965 MHz; 148 SMs from the device properties",
-    architecture_whitepaper_url=(
-        "measured: tcgen05.mma kind::f16 128x128x16 completes every 64 SM cycles (fp32 accumulate)"
-    ),
+    product_spec_url="https://www.nvidia.com/en-us/data-center/hgx/",
+    architecture_whitepaper_url="https://resources.nvidia.com/en-us-blackwell-architecture",
     fp16acc_rate_multiplier=1.0,
 )
 
@@ -254,31 +260,192 @@ def peaks_from_measurement(
 
 
 def load_measured_peaks(path: Path | None = None, *, device: int = 0) -> PeakResults:
-    """Read ``MEASURED_PEAKS.json`` and return the ceilings for CUDA device ``device``.
+    """Read a peak-measurement file and return the ceilings for CUDA device ``device``.
 
-    The file's ``gpu_name`` must match the device (a file measured on another
-    part is refused).
+    ``path`` defaults to the file named by the ``TKLAB_MEASURED_PEAKS``
+    environment variable.  The file's ``gpu_name`` must match the device (a
+    file measured on another part is refused).
 
     Raises:
-        FileNotFoundError: If the file is missing.
+        FileNotFoundError: If no file is named or it is missing.
         ValueError: If it does not describe this device.
         RuntimeError: If CUDA or the device is unavailable.
     """
     _validate_cuda_device(device)
-    source = path or DEFAULT_MEASURED_PEAKS
-    measured = read_json_object(source)
+    if path is None:
+        env = os.environ.get(MEASURED_PEAKS_ENV)
+        if not env:
+            raise FileNotFoundError(f"no peak-measurement file given and {MEASURED_PEAKS_ENV} is not set")
+        path = Path(env)
+    measured = read_json_object(path)
     gpu_name = torch.cuda.get_device_name(device)
     recorded = str(measured.get("gpu_name", ""))
     if recorded and recorded != gpu_name:
-        raise ValueError(f"{source}: measured on {recorded!r}, not on {gpu_name!r}")
+        raise ValueError(f"{path}: measured on {recorded!r}, not on {gpu_name!r}")
     major, minor = torch.cuda.get_device_capability(device)
     return peaks_from_measurement(
         measured,
         gpu_name=gpu_name,
         compute_capability=f"{major}.{minor}",
         torch_version=torch.__version__,
-        source=str(source),
+        source=str(path),
     )
+
+
+def _sample_max_sm_clock(device: int, stop: threading.Event, out: list[int]) -> None:
+    """Poll ``clocks.sm`` with nvidia-smi until ``stop`` is set (reads only)."""
+    while not stop.is_set():
+        try:
+            completed = subprocess.run(
+                ["nvidia-smi", f"--id={device}", "--query-gpu=clocks.sm", "--format=csv,noheader,nounits"],
+                check=True,
+                capture_output=True,
+                text=True,
+                timeout=10,
+            )
+            out.append(int(completed.stdout.strip().splitlines()[0]))
+        except (FileNotFoundError, subprocess.CalledProcessError, subprocess.TimeoutExpired, IndexError, ValueError):
+            return
+        stop.wait(0.2)
+
+
+def _event_ms(fn, reps: int) -> list[float]:
+    times = []
+    for _ in range(reps):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        end.synchronize()
+        times.append(start.elapsed_time(end))
+    return times
+
+
+def measure_peaks(
+    device: int,
+    *,
+    calibration_started_at_utc: str,
+    calibration_preflight_gpu_utilization_pct: tuple[int, ...],
+    calibration_preflight_gpu_utilization_limit_pct: int,
+    copy_elements: tuple[int, ...] = (1 << 27, 1 << 29),
+    gemm_sizes: tuple[int, ...] = (4096, 8192),
+    repetitions: int = 10,
+) -> PeakResults:
+    """Measure the empirical ceilings on ``device`` (``roofline.py:296-352`` of the reference).
+
+    Device-copy bandwidth (``b.copy_(a)`` of 16-bit buffers, read + write
+    bytes) and the cuBLAS fp16 GEMM rate with fp32 accumulation (``2 n^3``
+    FLOP), each the best of ``repetitions`` CUDA-event timings over a size
+    sweep; the theoretical ceilings are taken at the highest SM clock that
+    ``nvidia-smi`` reported during the GEMMs (the rated clock if it could
+    not be read).  Every sample is kept in the payload.
+    """
+    _validate_cuda_device(device)
+    gpu_name = torch.cuda.get_device_name(device)
+    profile = profile_for(gpu_name)
+    with torch.cuda.device(device):
+        bandwidth_samples = []
+        for n in copy_elements:
+            a = torch.empty(n, dtype=torch.float16, device="cuda").normal_()
+            b = torch.empty_like(a)
+            b.copy_(a)
+            best = min(_event_ms(lambda a=a, b=b: b.copy_(a), repetitions))
+            bandwidth_samples.append({"elements": n, "gbps": 2 * n * 2 / (best * 1e-3) / 1e9})
+            del a, b
+        clocks: list[int] = []
+        stop = threading.Event()
+        sampler = threading.Thread(target=_sample_max_sm_clock, args=(device, stop, clocks), daemon=True)
+        sampler.start()
+        gemm_samples = []
+        reduced = torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction
+        try:
+            torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+            for n in gemm_sizes:
+                x = torch.randn(n, n, dtype=torch.float16, device="cuda")
+                y = torch.randn(n, n, dtype=torch.float16, device="cuda")
+                torch.matmul(x, y)
+                best = min(_event_ms(lambda x=x, y=y: torch.matmul(x, y), repetitions))
+                gemm_samples.append({"n": n, "tflops": 2 * n**3 / (best * 1e-3) / 1e12})
+                del x, y
+            time.sleep(0.3)
+        finally:
+            torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = reduced
+            stop.set()
+            sampler.join(timeout=15)
+    clock = max(clocks) if clocks else profile.rated_boost_mhz
+    major, minor = torch.cuda.get_device_capability(device)
+    measured = {
+        "hbm_gbs": max(sample["gbps"] for sample in bandwidth_samples),
+        "bf16_tflops": max(sample["tflops"] for sample in gemm_samples),
+        "sm_max_mhz": clock,
+        "when": calibration_started_at_utc,
+        "how": "b.copy_(a) fp16 (read + write bytes) and torch.matmul fp16 with fp32 accumulation, best of "
+        f"{repetitions} CUDA-event timings per size",
+    }
+    peaks = peaks_from_measurement(
+        measured,
+        gpu_name=gpu_name,
+        compute_capability=f"{major}.{minor}",
+        torch_version=torch.__version__,
+        source="measured live",
+    )
+    peaks["calibration_preflight_gpu_utilization_pct"] = list(calibration_preflight_gpu_utilization_pct)
+    peaks["calibration_preflight_gpu_utilization_limit_pct"] = calibration_preflight_gpu_utilization_limit_pct
+    peaks["theoretical_provenance"]["bandwidth_samples"] = bandwidth_samples
+    peaks["theoretical_provenance"]["gemm_samples"] = gemm_samples
+    peaks["theoretical_provenance"]["sm_clock_samples_mhz"] = clocks
+    return peaks
+
+
+def load_or_measure_peaks(
+    results_root: Path,
+    *,
+    device: int = 0,
+    force: bool = False,
+    measured_peaks_path: Path | None = None,
+    calibration_started_at_utc: str | None = None,
+    calibration_preflight_gpu_utilization_pct: tuple[int, ...] = (),
+    calibration_preflight_gpu_utilization_limit_pct: int = 10,
+) -> tuple[PeakResults, Path]:
+    """Reuse a compatible ``<results_root>/<gpu-slug>/peaks.json`` or obtain and persist new ceilings.
+
+    New ceilings come from ``measured_peaks_path`` (or the file the
+    ``TKLAB_MEASURED_PEAKS`` environment variable names) when one is given,
+    otherwise from :func:`measure_peaks`.  A stored file is reused only when
+    it has this schema and describes this GPU, compute capability and torch
+    version.
+
+    Returns:
+        The ceilings and the path of ``peaks.json``.
+    """
+    _validate_cuda_device(device)
+    output_path = results_root / gpu_slug(device) / "peaks.json"
+    major, minor = torch.cuda.get_device_capability(device)
+    if output_path.exists() and not force:
+        stored = read_json_object(output_path)
+        expected = {
+            "schema_version": PEAKS_SCHEMA_VERSION,
+            "gpu_name": torch.cuda.get_device_name(device),
+            "compute_capability": f"{major}.{minor}",
+            "torch_version": torch.__version__,
+        }
+        if all(stored.get(key) == value for key, value in expected.items()):
+            return cast(PeakResults, stored), output_path
+    started = calibration_started_at_utc or datetime.now(timezone.utc).isoformat()
+    named = measured_peaks_path or (Path(os.environ[MEASURED_PEAKS_ENV]) if os.environ.get(MEASURED_PEAKS_ENV) else None)
+    if named is not None:
+        peaks = load_measured_peaks(named, device=device)
+        peaks["calibration_preflight_gpu_utilization_pct"] = list(calibration_preflight_gpu_utilization_pct)
+        peaks["calibration_preflight_gpu_utilization_limit_pct"] = calibration_preflight_gpu_utilization_limit_pct
+    else:
+        peaks = measure_peaks(
+            device,
+            calibration_started_at_utc=started,
+            calibration_preflight_gpu_utilization_pct=calibration_preflight_gpu_utilization_pct,
+            calibration_preflight_gpu_utilization_limit_pct=calibration_preflight_gpu_utilization_limit_pct,
+        )
+    write_json_atomic(output_path, cast(JsonObject, peaks))
+    return peaks, output_path
 
 
 class RooflinePoint(TypedDict):
