@@ -797,12 +797,15 @@ def run_decode(args: argparse.Namespace) -> None:
 
 
 def run_wide(args: argparse.Namespace) -> None:
-    """Forward for head dims above 128 (the 256-column kernel), 1 GPU, bf16.
+    """Forward and backward for head dims above 128, 1 GPU, bf16.
     Each shape: ``--warmup`` calls, then ``--steps`` back-to-back calls timed
     with CUDA events on the launching stream (Q, K and V are 134-268 MB each,
-    larger than L2).  FLOPs are the reference's forward model, 4·D per
-    attended pair; one JSON line per shape."""
-    from tklab.kernels.flash_attention import _launch_forward, check_device_status
+    larger than L2).  FLOPs are the reference's model, 4·D per attended pair
+    forward and 10·D backward; the backward is ``tk_attn_bwd_pre`` +
+    ``tk_attn_bwd_fused`` + ``tk_attn_dq_convert`` with each kernel timed on
+    its own; one JSON line per shape."""
+    from tklab import _native
+    from tklab.kernels.flash_attention import _NATIVE_DTYPE, _launch_forward, check_device_status
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
@@ -829,13 +832,54 @@ def run_wide(args: argparse.Namespace) -> None:
             torch.cuda.synchronize(device)
             ms = e0.elapsed_time(e1) / args.steps
             tflops = fwd_flops(batch, heads, seq, d, causal) / (ms * 1e-3) / 1e12
+            # Backward: three launches per call, each bracketed by events.
+            lib = _native.load()
+            do = torch.randn_like(q)
+            delta = torch.empty_like(lse)
+            dq_accum = torch.empty(q.shape, dtype=torch.float32, device=device)
+            dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+            sp = int(torch.cuda.current_stream(device).cuda_stream)
+            nd, scale, numel = _NATIVE_DTYPE[q.dtype], 1.0 / math.sqrt(d), q.numel()
+
+            def backward(ev=None) -> None:
+                if ev is not None:
+                    ev[0].record()
+                _native.check(lib.tk_attn_bwd_pre(o.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+                                                  batch, heads, seq, d, nd, sp), "bwd_pre")
+                if ev is not None:
+                    ev[1].record()
+                _native.check(lib.tk_attn_bwd_fused(q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
+                                                    lse.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+                                                    dk.data_ptr(), dv.data_ptr(), batch, heads, seq, d, nd,
+                                                    int(causal), scale, sp), "bwd_fused")
+                if ev is not None:
+                    ev[2].record()
+                _native.check(lib.tk_attn_dq_convert(dq_accum.data_ptr(), dq.data_ptr(), numel, nd, sp), "convert")
+                if ev is not None:
+                    ev[3].record()
+
+            for _ in range(args.warmup):
+                backward()
+            torch.cuda.synchronize(device)
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+            for ev in evs:
+                backward(ev)
+            torch.cuda.synchronize(device)
+            parts = [sum(ev[j].elapsed_time(ev[j + 1]) for ev in evs) / args.steps for j in range(3)]
+            bwd_ms = sum(parts)
+            bf = bwd_flops(batch, heads, seq, d, causal)
             print(json.dumps({
-                "wide_head_forward": True, "B": batch, "H": heads, "S": seq, "D": d, "causal": causal,
+                "wide_head": True, "B": batch, "H": heads, "S": seq, "D": d, "causal": causal,
                 "dtype": "bf16", "ms": round(ms, 4), "tflops": round(tflops, 1),
                 "frac_of_measured_bf16": round(tflops / peak, 3) if peak else None,
                 "kernel": "attn_fwd_d256_kernel (%d columns; D below it zero-filled)" % (192 if d <= 192 else 256),
+                "bwd_ms": round(bwd_ms, 4), "bwd_tflops": round(bf / (bwd_ms * 1e-3) / 1e12, 1),
+                "bwd_kernel_ms": {"attn_bwd_pre": round(parts[0], 4), "attn_bwd_d256": round(parts[1], 4),
+                                  "dq_convert": round(parts[2], 4)},
+                "bwd_fused_tflops": round(bf / (parts[1] * 1e-3) / 1e12, 1),
+                "bwd_fused_frac_of_measured_bf16": round(bf / (parts[1] * 1e-3) / 1e12 / peak, 3) if peak else None,
             }), flush=True)
-            del q, k, v, o, lse
+            del q, k, v, o, lse, do, delta, dq_accum, dq, dk, dv
     check_device_status()
 
 

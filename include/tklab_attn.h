@@ -66,7 +66,7 @@ extern "C" {
  * receives the base-2 log-sum-exp of every query row.  head_dim must be a
  * multiple of 8 from 8 to 256 (widths other than 64, 128 and 256 run the
  * next wider kernel with the missing columns zero-filled on load and clipped
- * on store; 136..256 run the 256-column kernel, which has no backward); q,
+ * on store; 136..192 run a 192-column and 200..256 a 256-column kernel); q,
  * k, v, o must be 16-byte aligned. */
 TK_API int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
@@ -81,7 +81,9 @@ TK_API int tk_attn_bwd_pre(const void* o, const void* d_o, float* delta, float* 
 /* Backward attention from the saved lse and the delta of tk_attn_bwd_pre.
  * dq_accum must hold zeros on entry (tk_attn_bwd_pre clears it); it is used
  * as an fp32 workspace and then converted into dq.  dk and dv are written
- * directly.  All of q, k, v, d_o, dq, dk, dv must be 16-byte aligned. */
+ * directly.  All of q, k, v, d_o, dq, dk, dv must be 16-byte aligned.
+ * head_dim: multiples of 8 up to 256 (136..256 on a kernel that gives each
+ * 128-key tile two CTAs, one per 128-column half of dk, dv and dq). */
 TK_API int tk_attn_bwd(const void* q, const void* k, const void* v, const void* d_o, const float* lse,
                 const float* delta, float* dq_accum, void* dq, void* dk, void* dv, int64_t batch,
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,

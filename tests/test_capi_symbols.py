@@ -62,13 +62,21 @@ def test_forward_rejects_bad_arguments_before_launch(kwargs: dict, status: int) 
 
 
 @pytest.mark.parametrize("head_dim", [136, 256])
-def test_backward_rejects_wide_heads(head_dim: int) -> None:
-    """136..256 have a forward kernel only: every backward entry refuses them as unsupported."""
+def test_deterministic_backward_rejects_wide_heads(head_dim: int) -> None:
+    """136..256 have a default backward only: the deterministic entries refuse them as unsupported."""
+    lib = _native.load()
+    p = 0x1000
+    assert lib.tk_attn_bwd_deterministic(p, p, p, p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
+    assert lib.tk_attn_bwd_dkdv(p, p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
+    assert lib.tk_attn_bwd_dq(p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
+
+
+@pytest.mark.parametrize("head_dim", [100, 264])
+def test_backward_rejects_unsupported_widths(head_dim: int) -> None:
     lib = _native.load()
     p = 0x1000
     assert lib.tk_attn_bwd_pre(p, p, p, p, 1, 2, 128, head_dim, 0, None) == 2
     assert lib.tk_attn_bwd(p, p, p, p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
-    assert lib.tk_attn_bwd_deterministic(p, p, p, p, p, p, p, p, p, p, 1, 2, 128, head_dim, 0, 0, 0.125, None) == 2
 
 
 def test_backward_rejects_missing_workspace() -> None:

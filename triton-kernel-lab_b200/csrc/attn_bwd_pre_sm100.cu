@@ -35,7 +35,7 @@ __device__ __forceinline__ float dot8(uint4 a, uint4 b, bool bf16) {
 }
 
 // Each group of G = DP/8 threads owns one row of d8 = head_dim/8 16-byte
-// chunks (d8 <= G; DP is 64 or 128, the padded width); thread g of the group
+// chunks (d8 <= G; DP is 64, 128 or 256, the padded width); thread g of the group
 // reads chunk g of O and dO (128-bit loads) and clears the matching 32 bytes
 // of the dQ accumulator, threads g >= d8 idle.
 template <int DP>
@@ -126,9 +126,14 @@ int grid_for(long long work, int threads) {
 
 int launch_attn_bwd_pre(const BwdPreArgs& a) {
   const long long rows = a.BH * a.S;
-  if (a.D < 8 || a.D > 128 || a.D % 8 != 0) return kErrUnsupported;
+  if (a.D < 8 || a.D > 256 || a.D % 8 != 0) return kErrUnsupported;
   const int d8 = static_cast<int>(a.D / 8);
-  if (a.D <= 64) {
+  if (a.D > 128) {
+    const int grid = grid_for(rows * 32, kPreThreads);
+    attn_bwd_pre_kernel<256><<<grid, kPreThreads, 0, a.stream>>>(
+        static_cast<const uint4*>(a.o), static_cast<const uint4*>(a.d_o), a.delta,
+        reinterpret_cast<float4*>(a.dq_accum), rows, d8, a.bf16 ? 1 : 0);
+  } else if (a.D <= 64) {
     const int grid = grid_for(rows * 8, kPreThreads);
     attn_bwd_pre_kernel<64><<<grid, kPreThreads, 0, a.stream>>>(
         static_cast<const uint4*>(a.o), static_cast<const uint4*>(a.d_o), a.delta,

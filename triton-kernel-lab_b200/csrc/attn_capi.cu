@@ -105,14 +105,15 @@ int make_map(CUtensorMap* map, const void* base, int64_t bh, int64_t seq, int64_
 // 3-D map over the contiguous fp32 (B*H, S, D) dQ accumulator: box
 // {32, 128, 1} (128-byte rows) with the 128-byte swizzle; used as the target
 // of TMA bulk reduce-add.
-int make_map_f32(CUtensorMap* map, const float* base, int64_t bh, int64_t seq, int64_t head_dim) {
+int make_map_f32(CUtensorMap* map, const float* base, int64_t bh, int64_t seq, int64_t head_dim,
+                 uint32_t box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return tk::kErrNoDriver;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(head_dim), static_cast<cuuint64_t>(seq),
                         static_cast<cuuint64_t>(bh)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_dim * 4),
                            static_cast<cuuint64_t>(seq * head_dim * 4)};
-  cuuint32_t box[3] = {32, 128, 1};
+  cuuint32_t box[3] = {32, box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -194,7 +195,7 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse
 int tk_attn_bwd_pre(const void* o, const void* d_o, float* delta, float* dq_accum, int64_t batch,
                     int64_t heads, int64_t seq, int64_t head_dim, int dtype, void* stream) {
   if (o == nullptr || d_o == nullptr || delta == nullptr) return tk::kErrInvalidArgument;
-  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype, 256)) return rc;
   if (!aligned16(o) || !aligned16(d_o)) return tk::kErrMisaligned;
   if (reinterpret_cast<uintptr_t>(delta) & 3u) return tk::kErrMisaligned;
   if (dq_accum != nullptr && !aligned16(dq_accum)) return tk::kErrMisaligned;
@@ -210,7 +211,7 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   if (q == nullptr || k == nullptr || v == nullptr || d_o == nullptr || lse == nullptr ||
       delta == nullptr || dq_accum == nullptr || dk == nullptr || dv == nullptr)
     return tk::kErrInvalidArgument;
-  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype, 256)) return rc;
   if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(d_o) || !aligned16(dk) ||
       !aligned16(dv) || !aligned16(dq_accum))
@@ -221,6 +222,19 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   if (int rc = status_ptr(&status)) return rc;
   const int64_t bh = batch * heads;
   CUtensorMap mq, mk, mv, mdo, mdk, mdv, mdq;
+  if (head_dim > 128) {
+    // 136..256: two CTAs per 128-key tile, one head-dim half each; 64-query steps.
+    if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype, 64)) return rc;
+    if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
+    if (int rc = make_map(&mdo, d_o, bh, seq, head_dim, dtype, 64)) return rc;
+    if (int rc = make_map(&mdk, dk, bh, seq, head_dim, dtype)) return rc;
+    if (int rc = make_map(&mdv, dv, bh, seq, head_dim, dtype)) return rc;
+    if (int rc = make_map_f32(&mdq, dq_accum, bh, seq, head_dim, 64)) return rc;
+    tk::BwdD256Args a{&mq, &mk, &mdo, &mdk, &mdv, &mdq, v, lse, delta, bh, seq, head_dim,
+                      dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale, scale * kLog2e, g_timeout_ns, status,
+                      static_cast<cudaStream_t>(stream)};
+    return tk::launch_attn_bwd_d256(a);
+  }
   if (int rc = make_map(&mq, q, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mk, k, bh, seq, head_dim, dtype)) return rc;
   if (int rc = make_map(&mv, v, bh, seq, head_dim, dtype)) return rc;
@@ -230,7 +244,7 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   if (int rc = make_map_f32(&mdq, dq_accum, bh, seq, head_dim)) return rc;
   tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, &mdq, lse, delta,
                 bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
-                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
+                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream), dk, dv};
   return tk::launch_attn_bwd(a);
 }
 
@@ -393,7 +407,7 @@ int tk_attn_bwd_dkdv(const void* q, const void* k, const void* v, const void* d_
   if (int rc = make_map(&mdv, dv, bh, seq, head_dim, dtype)) return rc;
   tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, nullptr, lse, delta,
                 bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
-                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
+                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream), dk, dv};
   return tk::launch_attn_bwd_dkdv(a);
 }
 
@@ -428,6 +442,17 @@ int tk_attn_bwd_deterministic(const void* q, const void* k, const void* v, const
                               const float* lse, float* delta, void* dq, void* dk, void* dv, int64_t batch,
                               int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
                               void* stream) {
+  // Everything the three launches check, before the first of them runs.
+  if (q == nullptr || k == nullptr || v == nullptr || o == nullptr || d_o == nullptr || lse == nullptr ||
+      delta == nullptr || dq == nullptr || dk == nullptr || dv == nullptr)
+    return tk::kErrInvalidArgument;
+  if (int rc = check_shape(batch, heads, seq, head_dim, dtype)) return rc;
+  if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
+  for (const void* p : {q, k, v, o, d_o, static_cast<const void*>(dq), static_cast<const void*>(dk),
+                        static_cast<const void*>(dv)})
+    if (!aligned16(p)) return tk::kErrMisaligned;
+  if ((reinterpret_cast<uintptr_t>(lse) & 3u) || (reinterpret_cast<uintptr_t>(delta) & 3u))
+    return tk::kErrMisaligned;
   if (int rc = tk_attn_bwd_pre(o, d_o, delta, nullptr, batch, heads, seq, head_dim, dtype, stream)) return rc;
   if (int rc = tk_attn_bwd_dkdv(q, k, v, d_o, lse, delta, dk, dv, batch, heads, seq, head_dim, dtype, causal,
                                 scale, stream))

@@ -75,6 +75,34 @@ struct BwdArgs {
   unsigned long long timeout_ns;
   int* status;
   cudaStream_t stream;
+  // dK and dV outputs, (B*H, S, D) 16-bit, stored row by row from registers.
+  // Last, so positional initialisers of the fields above stay valid.
+  void* dk = nullptr;
+  void* dv = nullptr;
+};
+
+// Backward for 128 < head_dim <= 256 (attn_bwd_d256_sm100.cu): Q and dO maps
+// with 64-row boxes, K, dK and dV maps with 128-row boxes, the fp32 dQ
+// accumulator map with {32, 64} boxes; V is read directly (row-major,
+// (B*H, S, D) 16-bit) into tensor memory.
+struct BwdD256Args {
+  const CUtensorMap* tm_q;
+  const CUtensorMap* tm_k;
+  const CUtensorMap* tm_do;
+  const CUtensorMap* tm_dk;
+  const CUtensorMap* tm_dv;
+  const CUtensorMap* tm_dq;
+  const void* v;
+  const float* lse;
+  const float* delta;
+  int64_t BH, S, D;
+  bool bf16;
+  int causal;
+  float scale;
+  float scale_log2;
+  unsigned long long timeout_ns;
+  int* status;
+  cudaStream_t stream;
 };
 
 // Deterministic dQ kernel (query-stationary, no atomics).
@@ -164,6 +192,7 @@ int launch_rope_rotate(const RopeRotateArgs& a);
 int launch_dq_convert_rope(const DqConvertRopeArgs& a);
 int launch_attn_bwd_pre(const BwdPreArgs& a);
 int launch_attn_bwd(const BwdArgs& a);
+int launch_attn_bwd_d256(const BwdD256Args& a);
 // The fused backward with its dQ path compiled out (dK and dV only; a.tm_dq
 // is not read).
 int launch_attn_bwd_dkdv(const BwdArgs& a);

@@ -16,16 +16,20 @@ Contract differences from the reference, all widenings:
 * head_dim any multiple of 8 from 8 to 128 (reference: 64 only,
   ``:283-284``); widths below 64 / 128 run the 64- / 128-column kernels with
   the tensor maps declaring the true width;
-* forward only, head_dim 136 to 256 (multiples of 8) on a 192-column
+* head_dim 136 to 256 (multiples of 8): the forward on a 192-column
   (136..192) or 256-column (200..256) kernel (one 128-row query tile per CTA
-  against 64-key tiles); the backward of those widths raises
-  ``NotImplementedError``.
+  against 64-key tiles), the backward on a 256-column kernel (two CTAs per
+  128-key tile, one head-dim half of dK/dV/dQ each, 64-query steps).  The
+  deterministic backward covers head_dim up to 128; for wider heads
+  deterministic mode raises (or warns, under ``warn_only``) as torch does
+  for ops without a deterministic implementation.
 """
 
 from __future__ import annotations
 
 import math
 import os
+import warnings
 from typing import Any, cast
 
 import torch
@@ -53,12 +57,14 @@ _HEADS = 16
 _HEAD_DIM = 64
 
 # Head dims the kernels accept: multiples of 8 (16-byte rows for TMA) up to
-# 128 for the forward and backward, up to 256 for the forward alone.  64, 128
-# and 256 are the kernels' native widths.
-MAX_HEAD_DIM = 128
+# 256, forward and backward.  64, 128 and 256 are the kernels' native widths
+# (the forward also has a 192-column one); the deterministic backward stops
+# at 128.
+MAX_HEAD_DIM = 256
 SUPPORTED_HEAD_DIMS = tuple(range(8, MAX_HEAD_DIM + 1, 8))
-MAX_FWD_HEAD_DIM = 256
-SUPPORTED_FWD_HEAD_DIMS = tuple(range(8, MAX_FWD_HEAD_DIM + 1, 8))
+MAX_FWD_HEAD_DIM = MAX_HEAD_DIM
+SUPPORTED_FWD_HEAD_DIMS = SUPPORTED_HEAD_DIMS
+MAX_DETERMINISTIC_HEAD_DIM = 128
 _NATIVE_DTYPE = {torch.float16: _native.TK_DTYPE_F16, torch.bfloat16: _native.TK_DTYPE_BF16}
 
 # Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile
@@ -86,8 +92,8 @@ _DETERMINISTIC_ENV = os.environ.get("TKLAB_DETERMINISTIC_BWD", "0") == "1"
 def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, max_head_dim: int = MAX_FWD_HEAD_DIM) -> None:
     """Validate the dense self-attention contract (same order as the reference, ``:267-288``).
 
-    ``max_head_dim`` is the widest head the calling path has a kernel for:
-    256 for the forward, 128 for the backward and the RoPE path.
+    ``max_head_dim`` is the widest head the calling path has a kernel for
+    (256 for the forward and the backward).
     """
     if q.ndim != 4 or k.ndim != 4 or v.ndim != 4:
         raise ValueError("attention expects Q, K, and V shaped (batch, heads, sequence, dim)")
@@ -228,7 +234,10 @@ def _launch_backward(
     ``TKLAB_DETERMINISTIC_BWD=1``) runs ``tk_attn_bwd_deterministic``
     instead: dK/dV from the fused kernel without its dQ path and dQ from a
     query-stationary kernel that sums the key tiles in one fixed order, so
-    repeated calls return bitwise identical gradients.
+    repeated calls return bitwise identical gradients.  That path covers
+    head_dim up to 128; a wider head under deterministic mode raises
+    ``RuntimeError`` (a warning and the default path under torch's
+    ``warn_only``).
     """
     if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
         raise ValueError("attention upstream gradient metadata must match Q")
@@ -243,6 +252,16 @@ def _launch_backward(
         raise ValueError("attention log-sum-exp buffer must be contiguous float32 BxHxN")
     if deterministic is None:
         deterministic = torch.are_deterministic_algorithms_enabled() or _DETERMINISTIC_ENV
+    if deterministic and head_dim > MAX_DETERMINISTIC_HEAD_DIM:
+        message = (
+            f"attention backward with head_dim {head_dim} does not have a deterministic implementation "
+            f"(the deterministic backward covers head_dim up to {MAX_DETERMINISTIC_HEAD_DIM})"
+        )
+        if torch.is_deterministic_algorithms_warn_only_enabled() and not _DETERMINISTIC_ENV:
+            warnings.warn(message, stacklevel=2)
+            deterministic = False
+        else:
+            raise RuntimeError(message)
     delta = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
