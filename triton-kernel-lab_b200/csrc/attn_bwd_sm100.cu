@@ -15,9 +15,8 @@
 // produced by the same CTA (10 N^2 d) and reduced across key tiles by the
 // TMA unit (bulk tensor reduce-add from shared memory).
 //
-// A CTA owns one 128-key tile at a time (K, V resident in smem) of one
-// (batch, head) and walks 128-query steps; the kernel is persistent (one
-// CTA per SM over balanced units of key tiles, below).  The transposed products are computed directly
+// One CTA owns a 128-key tile (K, V resident in smem) of one (batch, head)
+// and walks 128-query steps.  The transposed products are computed directly
 // (S^T = K Q^T, dP^T = V dO^T) so TMEM lane n holds key n.  16 warps in four
 // warpgroups, registers rebalanced with setmaxnreg:
 //   WG0  warp 0   producer: TMA for K, V, dO_i (1 stage); plain loads of
@@ -33,9 +32,7 @@
 //                     P^T, packed to 16 bits over the first half of the
 //                     warpgroup's own S^T columns for the dV MMA.  Phase 2:
 //                     dS^T = P^T (dP^T - delta) to smem for the dK and dQ
-//                     MMAs.  Tile epilogue: WG2 drains dV, WG3 dK from
-//                     TMEM into registers and stores its key row straight
-//                     to global memory while the next tile starts.
+//                     MMAs.  Epilogue: WG2 stores dV, WG3 stores dK.
 // MMA issue order per step i: dV_i, S_{i+1}, dQ_i, dK_i, dP_{i+1}, so the dS
 // warps compute P_{i+1} (the exp2-heavy phase) while dQ_i and dK_i run, and
 // the dQ warps drain dQ_i from TMEM while dK_i runs.
@@ -64,9 +61,8 @@ struct BwdCfg {
   static constexpr int kBarOff = kDeltaOff + 2 * 128 * 4;
   // kv_full, q_full[2], q_empty[2], do_full, do_empty, ld_full[2], ld_empty[2],
   // s_full, dp_full, p_ready, ds_ready, ds_empty, dq_full, dq_empty,
-  // stage_full[2], stage_free[2] (one per staging box), dkdv_done, kv_empty,
-  // tmem_drained
-  static constexpr int kNumBars = 1 + 4 + 2 + 4 + 14;
+  // stage_full[2], stage_free[2] (one per staging box), dkdv_done
+  static constexpr int kNumBars = 1 + 4 + 2 + 4 + 12;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
   static constexpr uint32_t kTmemCols = 512;
@@ -82,20 +78,40 @@ struct BwdCfg {
 
 constexpr int kBwdThreads = 512;
 // Launch allocation 128 registers x 512 threads = 65536; per warpgroup after
-// setmaxnreg: WG0 72 + WG1 152 + WG2 144 + WG3 144 = 512 x 128 threads, which
+// setmaxnreg: WG0 56 + WG1 152 + WG2 152 + WG3 152 = 512 x 128 threads, which
 // never exceeds the launch allocation (an inc beyond it would never return).
-// The control warpgroup's share holds the persistent MMA issue loop without
-// spilling.
 constexpr int kBwdLaunchRegs = 128;
-constexpr int kRegsCtrl = 72;
+constexpr int kRegsCtrl = 56;
 constexpr int kRegsDq = 152;
-constexpr int kRegsDs = 144;
+constexpr int kRegsDs = 152;
 static_assert(kRegsCtrl + kRegsDq + 2 * kRegsDs <= 4 * kBwdLaunchRegs, "register split exceeds the launch");
 
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, CtaControl* ctl,
                                           uint64_t timeout_ns, int* status, int site) {
   const bool ok = mbar_wait(bar, parity, ctl, timeout_ns, status, site);
   return __all_sync(0xffffffffu, ok);
+}
+
+// Stage one TMEM row (D fp32 values, times `mul`) as dtype into a swizzled
+// 128-row tile in smem, row `r`.
+template <int D, bool kBf16>
+__device__ __forceinline__ void stage_row(uint32_t t_row, uint8_t* tile, int r, float mul) {
+#pragma unroll
+  for (int cb = 0; cb < D / 32; ++cb) {
+    uint32_t v[32];
+    tmem_ld32(t_row + cb * 32, v);
+    tmem_wait_ld();
+    reg_fence(v);
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint4 w;
+      w.x = pack2<kBf16>(__uint_as_float(v[ch * 8 + 0]) * mul, __uint_as_float(v[ch * 8 + 1]) * mul);
+      w.y = pack2<kBf16>(__uint_as_float(v[ch * 8 + 2]) * mul, __uint_as_float(v[ch * 8 + 3]) * mul);
+      w.z = pack2<kBf16>(__uint_as_float(v[ch * 8 + 4]) * mul, __uint_as_float(v[ch * 8 + 5]) * mul);
+      w.w = pack2<kBf16>(__uint_as_float(v[ch * 8 + 6]) * mul, __uint_as_float(v[ch * 8 + 7]) * mul);
+      *reinterpret_cast<uint4*>(tile + swz_offset(r, cb * 32 + ch * 8, kTileRows)) = w;
+    }
+  }
 }
 
 // P^T for 32 queries of one key row: p = exp2(s * scale*log2(e) - LSE2[q]).
@@ -146,80 +162,17 @@ __device__ __forceinline__ void probs_chunk(const uint32_t (&sv)[32], const floa
   }
 }
 
-// Work units of the persistent kernel.  Causal: a head's key tiles j and
-// n_tiles-1-j form one unit (heavy tile first), so every unit walks
-// n_tiles + 1 query steps (the middle tile of an odd count is a unit alone);
-// non-causal: one key tile per unit.  Units are numbered head-major, so the
-// units resident at one time share a few heads' Q, dO and dQ lines in L2.
-__device__ __forceinline__ int bwd_unit_tiles(int u, int n_tiles, int causal) {
-  if (!causal) return 1;
-  const int p = u % ((n_tiles + 1) / 2);
-  return (p == n_tiles - 1 - p) ? 1 : 2;
-}
-
-__device__ __forceinline__ void bwd_unit_tile(int u, int sub, int n_tiles, int causal, int& bh, int& jn) {
-  if (!causal) {
-    bh = u / n_tiles;
-    jn = u % n_tiles;
-    return;
-  }
-  const int n_pairs = (n_tiles + 1) / 2;
-  bh = u / n_pairs;
-  const int p = u % n_pairs;
-  jn = (sub == 0) ? p : n_tiles - 1 - p;
-}
-
-// One row (key) of dV or dK, D fp32 values times `mul` read from TMEM at
-// t_row, converted to dtype in registers (d_real columns are kept).
-template <int D, bool kBf16>
-__device__ __forceinline__ void drain_row(uint32_t t_row, float mul, uint32_t (&w)[D / 2]) {
-#pragma unroll
-  for (int cb = 0; cb < D / 32; ++cb) {
-    uint32_t v[32];
-    tmem_ld32(t_row + cb * 32, v);
-    tmem_wait_ld();
-    reg_fence(v);
-#pragma unroll
-    for (int e = 0; e < 16; ++e)
-      w[cb * 16 + e] = pack2<kBf16>(__uint_as_float(v[2 * e]) * mul, __uint_as_float(v[2 * e + 1]) * mul);
-  }
-}
-
-// Store one drained row to global memory (row-major (B*H, S, d_real)
-// 16-bit): 32-byte stores when every row starts on a 32-byte boundary,
-// otherwise 16-byte stores; columns past d_real are skipped.
-template <int D>
-__device__ __forceinline__ void store_row(uint16_t* row, const uint32_t (&w)[D / 2], int d_real, bool wide) {
-#pragma unroll
-  for (int c = 0; c < D; c += 16) {
-    if (wide) {
-      if (c < d_real) st_global_v8(row + c, &w[c / 2]);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 2; ++q)
-        if (c + q * 8 < d_real)
-          *reinterpret_cast<uint4*>(row + c + q * 8) =
-              make_uint4(w[c / 2 + q * 4], w[c / 2 + q * 4 + 1], w[c / 2 + q * 4 + 2], w[c / 2 + q * 4 + 3]);
-    }
-  }
-}
-
 // kWithDq false compiles the dQ path out (no dQ product, drain or
 // reduction; tm_dq unused): the dK/dV half of the deterministic backward,
 // whose dQ comes from attn_bwd_dq_kernel.
-//
-// Persistent: one CTA per SM walks the units blockIdx.x, +gridDim.x, ...;
-// every role walks the same sequence of key tiles, and barrier phases follow
-// running counters (tiles and query steps done by this CTA), so one tile's
-// last steps, its dK/dV drain and the next tile's first products overlap.
 template <int D, bool kBf16, bool kWithDq>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const __grid_constant__ CUtensorMap tm_dq, uint16_t* __restrict__ dk_out,
-                    uint16_t* __restrict__ dv_out, const float* __restrict__ lse, const float* __restrict__ delta,
-                    int S, int n_tiles, int n_units, int causal, float scale, float scale_log2, int d_real,
-                    unsigned long long timeout_ns, int* status) {
+                    const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                    const __grid_constant__ CUtensorMap tm_dq, const float* __restrict__ lse,
+                    const float* __restrict__ delta, int S, int BH, int n_tiles, int causal, float scale,
+                    float scale_log2, int d_real, unsigned long long timeout_ns, int* status) {
   using C = BwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -229,6 +182,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int wg = warp >> 2;
+  // Head-major order: the key tiles of one (batch, head) are adjacent in the
+  // grid, so resident CTAs share a few heads' Q, dO and dQ-accumulator lines
+  // in L2.  Within a head the key tiles with the most query steps (smallest
+  // index under a causal mask) launch first.
+  const int bh = static_cast<int>(blockIdx.x) / n_tiles;
+  const int jn = static_cast<int>(blockIdx.x) % n_tiles;
+  const int n0 = jn * kTileRows;
+  const int i_start = causal ? jn : 0;
+  const int n_steps = n_tiles - i_start;
 
   uint8_t* sK = smem + C::kKOff;
   uint8_t* sV = smem + C::kVOff;
@@ -256,24 +218,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* stage_full = dq_empty + 1;  // [2]
   uint64_t* stage_free = stage_full + 2;  // [2]
   uint64_t* dkdv_done = stage_free + 2;
-  uint64_t* kv_empty = dkdv_done + 1;      // K, V of the tile no longer read
-  uint64_t* tmem_drained = kv_empty + 1;   // dK, dV of the tile read out of TMEM
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
-  // Query steps this CTA walks in all (read by the dQ warps, which need no
-  // other tile information).
-  uint32_t* total_steps = reinterpret_cast<uint32_t*>(smem + C::kCtlOff + 32);
 
   if (threadIdx.x == 0) {
-    uint32_t n_total = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const int n_sub = bwd_unit_tiles(u, n_tiles, causal);
-      for (int sub = 0; sub < n_sub; ++sub) {
-        int bh, jn;
-        bwd_unit_tile(u, sub, n_tiles, causal, bh, jn);
-        n_total += n_tiles - (causal ? jn : 0);
-      }
-    }
-    *total_steps = n_total;
     mbar_init(kv_full, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
@@ -295,8 +242,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&stage_free[i], 1);
     }
     mbar_init(dkdv_done, 1);
-    mbar_init(kv_empty, 1);
-    mbar_init(tmem_drained, 8);
     ctl->abort = 0;
     fence_mbarrier_init();
   }
@@ -305,6 +250,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tma_prefetch_map(&tm_k);
     tma_prefetch_map(&tm_v);
     tma_prefetch_map(&tm_do);
+    tma_prefetch_map(&tm_dk);
+    tma_prefetch_map(&tm_dv);
     tma_prefetch_map(&tm_dq);
   }
   if (warp == 1) tmem_alloc(&ctl->tmem_base, C::kTmemCols);
@@ -312,79 +259,56 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
+  const size_t row_base = static_cast<size_t>(bh) * S;
 
   if (wg == 0) {
     warpgroup_reg_dec<kRegsCtrl>();
     if (warp == 3) {
       // ---------------- Q producer (its own warp so a Q load never waits
-      // behind the dO or LSE waits; it runs ahead into the next tile) ----------------
-      uint32_t g = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const int n_sub = bwd_unit_tiles(u, n_tiles, causal);
-        for (int sub = 0; ok && sub < n_sub; ++sub) {
-          int bh, jn;
-          bwd_unit_tile(u, sub, n_tiles, causal, bh, jn);
-          const int i_start = causal ? jn : 0;
-          for (int i = i_start; i < n_tiles; ++i, ++g) {
-            const int st = g & 1;
-            if (!(ok = warp_wait(&q_empty[st], ((g >> 1) & 1) ^ 1, ctl, timeout_ns, status, 1))) break;
-            if (lane == 0) {
-              mbar_arrive_expect_tx(&q_full[st], C::kTileBytes);
+      // behind the dO or LSE waits) ----------------
+      for (int it = 0; it < n_steps; ++it) {
+        const int m0 = (i_start + it) * kTileRows;
+        const int st = it & 1;
+        if (!warp_wait(&q_empty[st], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 1)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&q_full[st], C::kTileBytes);
 #pragma unroll
-              for (int b = 0; b < D / 64; ++b)
-                tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, i * kTileRows, bh);
-            }
-          }
+          for (int b = 0; b < D / 64; ++b)
+            tma_load_3d(sQ + st * C::kTileBytes + b * kBlockBytes, &tm_q, &q_full[st], b * 64, m0, bh);
         }
       }
     } else if (warp == 0) {
       // ---------------- K/V, dO and LSE/delta producer ----------------
-      uint32_t g = 0;
-      int tc = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const int n_sub = bwd_unit_tiles(u, n_tiles, causal);
-        for (int sub = 0; ok && sub < n_sub; ++sub, ++tc) {
-          int bh, jn;
-          bwd_unit_tile(u, sub, n_tiles, causal, bh, jn);
-          const int n0 = jn * kTileRows;
-          const int i_start = causal ? jn : 0;
-          const size_t row_base = static_cast<size_t>(bh) * S;
-          // K and V of this tile once the previous tile's products are done.
-          if (tc > 0 && !(ok = warp_wait(kv_empty, (tc - 1) & 1, ctl, timeout_ns, status, 19))) break;
-          if (lane == 0) {
-            mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(kv_full, 2 * C::kTileBytes);
 #pragma unroll
-            for (int b = 0; b < D / 64; ++b) {
-              tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
-              tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
-            }
-          }
-          for (int i = i_start; i < n_tiles; ++i, ++g) {
-            const int m0 = i * kTileRows;
-            if (!(ok = warp_wait(do_empty, (g & 1) ^ 1, ctl, timeout_ns, status, 2))) break;
-            if (lane == 0) {
-              mbar_arrive_expect_tx(do_full, C::kTileBytes);
-#pragma unroll
-              for (int b = 0; b < D / 64; ++b) tma_load_3d(sDO + b * kBlockBytes, &tm_do, do_full, b * 64, m0, bh);
-            }
-            // -LSE / delta for this query step (LSE stored negated for the
-            // packed P argument).  Padded queries get -LSE = -inf so their
-            // probabilities are exactly zero.
-            const int lb = g & 1;
-            if (!(ok = warp_wait(&ld_empty[lb], ((g >> 1) & 1) ^ 1, ctl, timeout_ns, status, 3))) break;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int q = e * 32 + lane;
-              const int mg = m0 + q;
-              const bool valid = mg < S;
-              sLse[lb * 128 + q] = valid ? -lse[row_base + mg] : -INFINITY;
-              sDelta[lb * 128 + q] = valid ? delta[row_base + mg] : 0.0f;
-            }
-            mbar_arrive(&ld_full[lb]);
-          }
+        for (int b = 0; b < D / 64; ++b) {
+          tma_load_3d(sK + b * kBlockBytes, &tm_k, kv_full, b * 64, n0, bh);
+          tma_load_3d(sV + b * kBlockBytes, &tm_v, kv_full, b * 64, n0, bh);
         }
+      }
+      for (int it = 0; it < n_steps; ++it) {
+        const int m0 = (i_start + it) * kTileRows;
+        if (!warp_wait(do_empty, (it & 1) ^ 1, ctl, timeout_ns, status, 2)) break;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(do_full, C::kTileBytes);
+#pragma unroll
+          for (int b = 0; b < D / 64; ++b) tma_load_3d(sDO + b * kBlockBytes, &tm_do, do_full, b * 64, m0, bh);
+        }
+        // -LSE / delta for this query step (LSE stored negated for the
+        // packed P argument).  Padded queries get -LSE = -inf so their
+        // probabilities are exactly zero.
+        const int lb = it & 1;
+        if (!warp_wait(&ld_empty[lb], ((it >> 1) & 1) ^ 1, ctl, timeout_ns, status, 3)) break;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int q = e * 32 + lane;
+          const int mg = m0 + q;
+          const bool valid = mg < S;
+          sLse[lb * 128 + q] = valid ? -lse[row_base + mg] : -INFINITY;
+          sDelta[lb * 128 + q] = valid ? delta[row_base + mg] : 0.0f;
+        }
+        mbar_arrive(&ld_full[lb]);
       }
     } else if (warp == 1) {
       // ---------------- MMA issuer ----------------
@@ -397,29 +321,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t idesc_s = idesc_f16(fmt, 128, 128, 0, 0);
       const uint32_t idesc_kv = idesc_f16(fmt, 128, D, 0, 1);
       const uint32_t idesc_dq = idesc_f16(fmt, 128, D, 1, 1);
-      // Every operand tile sits at a compile-time offset from the 1024-byte
-      // aligned shared-memory base, so each descriptor low word is one
-      // register (the base in 16-byte units) plus a constant.
-      const uint32_t sw = smem_u32(smem) >> 4;
-      constexpr uint32_t kKm = (16u >> 4) << 16;                          // K-major leading offset field
-      constexpr uint32_t kMn = ((kTileRows * kSwizzleBytes) >> 4) << 16;  // MN-major leading offset field
-      const uint32_t k_lo = sw + ((C::kKOff >> 4) | kKm);
-      const uint32_t k_mn_lo = sw + ((C::kKOff >> 4) | kMn);
-      const uint32_t v_lo = sw + ((C::kVOff >> 4) | kKm);
-      const uint32_t ds_lo = sw + ((C::kDSOff >> 4) | kKm);
-      const uint32_t ds_mn_lo = sw + ((C::kDSOff >> 4) | kMn);
-      const uint32_t do_lo = sw + ((C::kDOOff >> 4) | kKm);
-      const uint32_t do_mn_lo = sw + ((C::kDOOff >> 4) | kMn);
-      const uint32_t q_lo0 = sw + ((C::kQOff >> 4) | kKm);
-      const uint32_t q_mn_lo0 = sw + ((C::kQOff >> 4) | kMn);
+      const uint32_t k_lo = sdesc_lo_kmajor(smem_u32(sK));
+      const uint32_t k_mn_lo = sdesc_lo_mnmajor(smem_u32(sK), kTileRows);
+      const uint32_t v_lo = sdesc_lo_kmajor(smem_u32(sV));
+      const uint32_t ds_lo = sdesc_lo_kmajor(smem_u32(sDS));
+      const uint32_t ds_mn_lo = sdesc_lo_mnmajor(smem_u32(sDS), kTileRows);
+      const uint32_t do_lo = sdesc_lo_kmajor(smem_u32(sDO));
+      const uint32_t do_mn_lo = sdesc_lo_mnmajor(smem_u32(sDO), kTileRows);
+      const uint32_t q_lo0 = sdesc_lo_kmajor(smem_u32(sQ));
+      const uint32_t q_mn_lo0 = sdesc_lo_mnmajor(smem_u32(sQ), kTileRows);
       constexpr uint32_t kTileLo = C::kTileBytes >> 4;  // low-word step between Q stages
       auto commit = [&](uint64_t* bar) {
         if (leader) umma_commit(bar);
         __syncwarp();
       };
-      auto issue_s = [&](uint32_t g) -> bool {
-        const int st = g & 1;
-        if (!warp_wait(&q_full[st], (g >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
+      auto issue_s = [&](int it) -> bool {
+        const int st = it & 1;
+        if (!warp_wait(&q_full[st], (it >> 1) & 1, ctl, timeout_ns, status, 4)) return false;
         tc_fence_after();
         const uint32_t q_lo = q_lo0 + st * kTileLo;
         if (leader) {
@@ -432,10 +350,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         return true;
       };
-      auto issue_dp = [&](uint32_t g) -> bool {
-        if (!warp_wait(do_full, g & 1, ctl, timeout_ns, status, 5)) return false;
-        if (kWithDq && C::kDqAliased && g > 0) {
-          if (!warp_wait(dq_empty, (g - 1) & 1, ctl, timeout_ns, status, 6)) return false;
+      auto issue_dp = [&](int it) -> bool {
+        if (!warp_wait(do_full, it & 1, ctl, timeout_ns, status, 5)) return false;
+        if (kWithDq && C::kDqAliased && it > 0) {
+          if (!warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 6)) return false;
         }
         tc_fence_after();
         if (leader) {
@@ -448,121 +366,99 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __syncwarp();
         return true;
       };
-      uint32_t g = 0;
-      int tc = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const int n_sub = bwd_unit_tiles(u, n_tiles, causal);
-        for (int sub = 0; ok && sub < n_sub; ++sub, ++tc) {
-          int bh, jn;
-          bwd_unit_tile(u, sub, n_tiles, causal, bh, jn);
-          const int n_steps = n_tiles - (causal ? jn : 0);
-          if (!(ok = warp_wait(kv_full, tc & 1, ctl, timeout_ns, status, 7))) break;
-          if (!(ok = issue_s(g) && issue_dp(g))) break;
-          for (int it = 0; it < n_steps; ++it, ++g) {
-            const int st = g & 1;
-            const uint32_t q_mn_lo = q_mn_lo0 + st * kTileLo;
-            // dV += P^T dO.  P^T of queries 64h..64h+63 sits packed in the
-            // first 32 columns of warpgroup h's 64 S columns.  The tile's
-            // first dV product overwrites dV (and its first dK product dK):
-            // the previous tile's must have been read out first.
-            if (!(ok = warp_wait(p_ready, g & 1, ctl, timeout_ns, status, 8))) break;
-            if (it == 0 && tc > 0 && !(ok = warp_wait(tmem_drained, (tc - 1) & 1, ctl, timeout_ns, status, 20))) break;
-            tc_fence_after();
-            if (leader) {
+      bool ok = warp_wait(kv_full, 0, ctl, timeout_ns, status, 7);
+      if (ok && n_steps > 0) ok = issue_s(0) && issue_dp(0);
+      for (int it = 0; ok && it < n_steps; ++it) {
+        const int st = it & 1;
+        const uint32_t q_mn_lo = q_mn_lo0 + st * kTileLo;
+        // dV += P^T dO.  P^T of queries 64h..64h+63 sits packed in the
+        // first 32 columns of warpgroup h's 64 S columns.
+        if (!(ok = warp_wait(p_ready, it & 1, ctl, timeout_ns, status, 8))) break;
+        tc_fence_after();
+        if (leader) {
 #pragma unroll
-              for (int kk = 0; kk < kTileRows / 16; ++kk)
-                umma_ts_w(tmem + C::kColDV, tmem + C::kColS + (kk >> 2) * 64 + (kk & 3) * 8,
-                          do_mn_lo + mnmajor_koff(kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-              umma_commit(do_empty);
-            }
-            __syncwarp();
-            if (it + 1 < n_steps && !(ok = issue_s(g + 1))) break;
-            // dQ = dS K  (dS in smem from the dS warps)
-            if (!(ok = warp_wait(ds_ready, g & 1, ctl, timeout_ns, status, 9))) break;
-            tc_fence_after();
-            if constexpr (kWithDq) {
-              if (!C::kDqAliased && g > 0) {
-                if (!(ok = warp_wait(dq_empty, (g - 1) & 1, ctl, timeout_ns, status, 10))) break;
-              }
-              if (leader) {
-#pragma unroll
-                for (int kk = 0; kk < kTileRows / 16; ++kk)
-                  umma_ss_w(tmem + C::kColDQ, ds_mn_lo + mnmajor_koff(kk * 16), k_mn_lo + mnmajor_koff(kk * 16),
-                            idesc_dq, kk > 0 ? 1u : 0u);
-                umma_commit(dq_full);
-              }
-              __syncwarp();
-            }
-            // dK += dS^T Q; the smem dS tile is free after this one.
-            if (leader) {
-#pragma unroll
-              for (int kk = 0; kk < kTileRows / 16; ++kk)
-                umma_ss_w(tmem + C::kColDK, ds_lo + kmajor_koff(kTileRows, kk * 16), q_mn_lo + mnmajor_koff(kk * 16),
-                          idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
-              umma_commit(&q_empty[st]);
-              umma_commit(ds_empty);
-            }
-            __syncwarp();
-            if (it + 1 < n_steps && !(ok = issue_dp(g + 1))) break;
-          }
-          if (!ok) break;
-          // The tile's products are all issued: dK and dV are final once they
-          // complete, and K / V may be replaced.
-          commit(dkdv_done);
-          commit(kv_empty);
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ts_w(tmem + C::kColDV, tmem + C::kColS + (kk >> 2) * 64 + (kk & 3) * 8,
+                      do_mn_lo + mnmajor_koff(kk * 16), idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(do_empty);
         }
+        __syncwarp();
+        if (it + 1 < n_steps && !(ok = issue_s(it + 1))) break;
+        // dQ = dS K  (dS in smem from the dS warps)
+        if (!(ok = warp_wait(ds_ready, it & 1, ctl, timeout_ns, status, 9))) break;
+        tc_fence_after();
+        if constexpr (kWithDq) {
+          if (!C::kDqAliased && it > 0) {
+            if (!(ok = warp_wait(dq_empty, (it - 1) & 1, ctl, timeout_ns, status, 10))) break;
+          }
+          if (leader) {
+#pragma unroll
+            for (int kk = 0; kk < kTileRows / 16; ++kk)
+              umma_ss_w(tmem + C::kColDQ, ds_mn_lo + mnmajor_koff(kk * 16), k_mn_lo + mnmajor_koff(kk * 16), idesc_dq,
+                        kk > 0 ? 1u : 0u);
+            umma_commit(dq_full);
+          }
+          __syncwarp();
+        }
+        // dK += dS^T Q; the smem dS tile is free after this one.
+        if (leader) {
+#pragma unroll
+          for (int kk = 0; kk < kTileRows / 16; ++kk)
+            umma_ss_w(tmem + C::kColDK, ds_lo + kmajor_koff(kTileRows, kk * 16), q_mn_lo + mnmajor_koff(kk * 16),
+                      idesc_kv, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&q_empty[st]);
+          umma_commit(ds_empty);
+        }
+        __syncwarp();
+        if (it + 1 < n_steps && !(ok = issue_dp(it + 1))) break;
       }
+      if (ok) commit(dkdv_done);
     } else if (warp == 2 && kWithDq) {
       // ---------------- dQ reduce issuer ----------------
       // Box by box: each 32-column box is reduced as soon as it is staged,
       // and released once the TMA has read it (checked one reduction later,
       // so that a box is being read while the other is being filled).
-      // Boxes alternate between the two staging buffers, so box n uses
-      // buffer n & 1 and is its (n >> 1)-th use.
       bool ok = true;
-      uint32_t box_n = 0;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-        const int n_sub = bwd_unit_tiles(u, n_tiles, causal);
-        for (int sub = 0; ok && sub < n_sub; ++sub) {
-          int bh, jn;
-          bwd_unit_tile(u, sub, n_tiles, causal, bh, jn);
-          for (int m0 = (causal ? jn : 0) * kTileRows; ok && m0 < n_tiles * kTileRows; m0 += kTileRows) {
-            for (int col = 0; col < D; col += 32, ++box_n) {
-              const int bx = box_n & 1;
-              if (!(ok = warp_wait(&stage_full[bx], (box_n >> 1) & 1, ctl, timeout_ns, status, 18))) break;
-              if (lane == 0) {
-                // A head_dim below the kernel's width leaves whole boxes past
-                // the tensor's last column: nothing to add there (the group
-                // stays, empty, so that the count of groups in flight holds).
-                if (col < d_real)
-                  tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, col, m0, bh);
-                tma_store_commit();
-                tma_store_wait_read_le1();
-                if (box_n > 0) mbar_arrive(&stage_free[bx ^ 1]);  // the previous box, in the other buffer
-              }
-              __syncwarp();
+      int prev = -1;
+      for (int it = 0; ok && it < n_steps; ++it) {
+        const int m0 = (i_start + it) * kTileRows;
+#pragma unroll
+        for (int pass = 0; pass < C::kDqPasses; ++pass) {
+          const uint32_t cnt = static_cast<uint32_t>(it * C::kDqPasses + pass);
+#pragma unroll
+          for (int bx = 0; bx < 2; ++bx) {
+            if (!(ok = warp_wait(&stage_full[bx], cnt & 1, ctl, timeout_ns, status, 18))) break;
+            if (lane == 0) {
+              // A head_dim below the kernel's width leaves whole boxes past
+              // the tensor's last column: nothing to add there (the group
+              // stays, empty, so that the count of groups in flight holds).
+              if (pass * 64 + bx * 32 < d_real)
+                tma_reduce_add_3d(&tm_dq, sDQ + bx * kTileRows * kSwizzleBytes, pass * 64 + bx * 32, m0, bh);
+              tma_store_commit();
+              tma_store_wait_read_le1();
+              if (prev >= 0) mbar_arrive(&stage_free[prev]);
             }
+            prev = bx;
+            __syncwarp();
           }
+          if (!ok) break;
         }
       }
       if (lane == 0) {
         tma_store_wait_read_all();
-        if (ok && box_n > 0) mbar_arrive(&stage_free[(box_n - 1) & 1]);
+        if (ok && prev >= 0) mbar_arrive(&stage_free[prev]);
         tma_store_wait_all();
       }
     }
   } else if (wg == 1) {
     warpgroup_reg_inc<kRegsDq>();
-    // ---------------- dQ warps: thread r owns query m0 + r of every step ----------------
+    // ---------------- dQ warps: thread r owns query m0 + r ----------------
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
-    // Every step of every tile of this CTA, in order.
-    const uint32_t n_total = *total_steps;
     bool ok = true;
-    for (uint32_t g = 0; kWithDq && ok && g < n_total; ++g) {
-      if (!(ok = warp_wait(dq_full, g & 1, ctl, timeout_ns, status, 16))) break;
+    for (int it = 0; kWithDq && ok && it < n_steps; ++it) {
+      if (!(ok = warp_wait(dq_full, it & 1, ctl, timeout_ns, status, 16))) break;
       tc_fence_after();
       uint32_t v[D / 32][32];
 #pragma unroll
@@ -575,7 +471,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       if (lane == 0) mbar_arrive(dq_empty);
 #pragma unroll
       for (int pass = 0; pass < C::kDqPasses; ++pass) {
-        const uint32_t cnt = g * C::kDqPasses + pass;
+        const uint32_t cnt = static_cast<uint32_t>(it * C::kDqPasses + pass);
 #pragma unroll
         for (int bx = 0; bx < 2; ++bx) {
           if (!(ok = warp_wait(&stage_free[bx], (cnt & 1) ^ 1, ctl, timeout_ns, status, 17))) break;
@@ -597,130 +493,125 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else {
     warpgroup_reg_inc<kRegsDs>();
-    // ---------------- dS warps: thread t owns key n0 + t of each tile ----------------
+    // ---------------- dS warps: thread t owns key n0 + t ----------------
     const int h = wg - 2;  // query half of the step owned by this warpgroup
     const int q4 = warp & 3;
     const int t = q4 * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q4 * 32) << 16);
     const uint32_t s_cols = t_lane + C::kColS + h * 64;
     const uint32_t dp_cols = t_lane + C::kColDP + h * 64;
-    // 32-byte dK / dV stores when every row starts on a 32-byte boundary.
-    uint16_t* out = (h == 0) ? dv_out : dk_out;
-    const bool wide = (d_real % 16) == 0 && (reinterpret_cast<uintptr_t>(out) & 31u) == 0;
-    uint32_t g = 0;
-    int tc = 0;
+    const bool key_ok = (n0 + t) < S;
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
-      const int n_sub = bwd_unit_tiles(u, n_tiles, causal);
-      for (int sub = 0; ok && sub < n_sub; ++sub, ++tc) {
-        int bh, jn;
-        bwd_unit_tile(u, sub, n_tiles, causal, bh, jn);
-        const int n0 = jn * kTileRows;
-        const bool key_ok = (n0 + t) < S;
-        for (int i = causal ? jn : 0; i < n_tiles; ++i, ++g) {
-          const int lb = g & 1;
-          if (!(ok = warp_wait(&ld_full[lb], (g >> 1) & 1, ctl, timeout_ns, status, 11))) break;
-          if (!(ok = warp_wait(s_full, g & 1, ctl, timeout_ns, status, 12))) break;
-          tc_fence_after();
-          const bool diag = causal && (i == jn);
-          const float* nlse_s = sLse + lb * 128 + h * 64;
-          const float* del_s = sDelta + lb * 128 + h * 64;
-          // Phase 1: P^T for this warpgroup's 64 queries -> registers and,
-          // packed to 16 bits, back over the first 32 of its S columns (both
-          // 32-column chunks are read before any packed half is written).
-          float p[2][32];
-          const bool masked = __any_sync(0xffffffffu, diag || !key_ok);
-          {
-            // Both 32-column loads are in flight together.
-            uint32_t sv[2][32];
-            tmem_ld32(s_cols, sv[0]);
-            tmem_ld32(s_cols + 32, sv[1]);
-            tmem_wait_ld();
-            reg_fence(sv[0]);
-            reg_fence(sv[1]);
+    for (int it = 0; it < n_steps; ++it) {
+      const int i = i_start + it;
+      const int lb = it & 1;
+      if (!(ok = warp_wait(&ld_full[lb], (it >> 1) & 1, ctl, timeout_ns, status, 11))) break;
+      if (!(ok = warp_wait(s_full, it & 1, ctl, timeout_ns, status, 12))) break;
+      tc_fence_after();
+      const bool diag = causal && (i == jn);
+      const float* nlse_s = sLse + lb * 128 + h * 64;
+      const float* del_s = sDelta + lb * 128 + h * 64;
+      // Phase 1: P^T for this warpgroup's 64 queries -> registers and,
+      // packed to 16 bits, back over the first 32 of its S columns (both
+      // 32-column chunks are read before any packed half is written).
+      float p[2][32];
+      const bool masked = __any_sync(0xffffffffu, diag || !key_ok);
+      {
+        // Both 32-column loads are in flight together.
+        uint32_t sv[2][32];
+        tmem_ld32(s_cols, sv[0]);
+        tmem_ld32(s_cols + 32, sv[1]);
+        tmem_wait_ld();
+        reg_fence(sv[0]);
+        reg_fence(sv[1]);
 #pragma unroll
-            for (int c = 0; c < 2; ++c) {
-              if (masked)
-                probs_chunk<true>(sv[c], nlse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
-              else
-                probs_chunk<false>(sv[c], nlse_s + c * 32, scale_log2, 0, 0, true, p[c]);
-            }
-          }
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t pp[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
-            tmem_st16(s_cols + c * 16, pp);
-          }
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(p_ready);
-          // Phase 2: dS^T = P^T (dP^T - delta) -> smem for the dK and dQ MMAs.
-          if (!(ok = warp_wait(dp_full, g & 1, ctl, timeout_ns, status, 13))) break;
-          if (g > 0) {
-            if (!(ok = warp_wait(ds_empty, (g - 1) & 1, ctl, timeout_ns, status, 14))) break;
-          }
-          tc_fence_after();
-          uint32_t dpv2[2][32];
-          tmem_ld32(dp_cols, dpv2[0]);
-          tmem_ld32(dp_cols + 32, dpv2[1]);
-          tmem_wait_ld();
-          reg_fence(dpv2[0]);
-          reg_fence(dpv2[1]);
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const uint32_t (&dpv)[32] = dpv2[c];
-            uint32_t dd[16];
-            const float4* del4 = reinterpret_cast<const float4*>(del_s + c * 32);
-            const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
-#pragma unroll
-            for (int e4 = 0; e4 < 8; ++e4) {
-              const float4 dl = del4[e4];  // one broadcast 128-bit load for 4 queries
-              const int e = e4 * 4;
-              // dS = P (dP - delta), two queries per packed instruction.
-              float d0, d1, d2, d3;
-              f2_unpack(fmul2(f2_pack(p[c][e], p[c][e + 1]),
-                              ffma2(f2_pack(dl.x, dl.y), neg1,
-                                    f2_pack(__uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1])))),
-                        d0, d1);
-              f2_unpack(fmul2(f2_pack(p[c][e + 2], p[c][e + 3]),
-                              ffma2(f2_pack(dl.z, dl.w), neg1,
-                                    f2_pack(__uint_as_float(dpv[e + 2]), __uint_as_float(dpv[e + 3])))),
-                        d2, d3);
-              dd[e4 * 2] = pack2<kBf16>(d0, d1);
-              dd[e4 * 2 + 1] = pack2<kBf16>(d2, d3);
-            }
-#pragma unroll
-            for (int w = 0; w < 4; ++w) {
-              uint4 v = make_uint4(dd[w * 4 + 0], dd[w * 4 + 1], dd[w * 4 + 2], dd[w * 4 + 3]);
-              *reinterpret_cast<uint4*>(sDS + swz_offset(t, h * 64 + c * 32 + w * 8, kTileRows)) = v;
-            }
-          }
-          fence_proxy_async_smem();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&ld_empty[lb]);
-            mbar_arrive(ds_ready);
-          }
+        for (int c = 0; c < 2; ++c) {
+          if (masked)
+            probs_chunk<true>(sv[c], nlse_s + c * 32, scale_log2, h * 64 + c * 32, diag ? t : 0, key_ok, p[c]);
+          else
+            probs_chunk<false>(sv[c], nlse_s + c * 32, scale_log2, 0, 0, true, p[c]);
         }
-        if (!ok) break;
-        // Tile epilogue: WG2 reads dV, WG3 dK (scaled) out of TMEM into
-        // registers, hands the columns back to the MMA warp, then stores
-        // its key row straight to global memory (rows past the sequence and
-        // columns past head_dim skipped) while the next tile's first
-        // products run.
-        if (!(ok = warp_wait(dkdv_done, tc & 1, ctl, timeout_ns, status, 15))) break;
-        tc_fence_after();
-        uint32_t w[D / 2];
-        drain_row<D, kBf16>(t_lane + (h == 0 ? C::kColDV : C::kColDK), h == 0 ? 1.0f : scale, w);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(tmem_drained);
-        if (key_ok) store_row<D>(out + (static_cast<size_t>(bh) * S + n0 + t) * d_real, w, d_real, wide);
       }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pp[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) pp[e] = pack2<kBf16>(p[c][2 * e], p[c][2 * e + 1]);
+        tmem_st16(s_cols + c * 16, pp);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_ready);
+      // Phase 2: dS^T = P^T (dP^T - delta) -> smem for the dK and dQ MMAs.
+      if (!(ok = warp_wait(dp_full, it & 1, ctl, timeout_ns, status, 13))) break;
+      if (it > 0) {
+        if (!(ok = warp_wait(ds_empty, (it - 1) & 1, ctl, timeout_ns, status, 14))) break;
+      }
+      tc_fence_after();
+      uint32_t dpv2[2][32];
+      tmem_ld32(dp_cols, dpv2[0]);
+      tmem_ld32(dp_cols + 32, dpv2[1]);
+      tmem_wait_ld();
+      reg_fence(dpv2[0]);
+      reg_fence(dpv2[1]);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t (&dpv)[32] = dpv2[c];
+        uint32_t dd[16];
+        const float4* del4 = reinterpret_cast<const float4*>(del_s + c * 32);
+        const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+#pragma unroll
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 dl = del4[e4];  // one broadcast 128-bit load for 4 queries
+          const int e = e4 * 4;
+          // dS = P (dP - delta), two queries per packed instruction.
+          float d0, d1, d2, d3;
+          f2_unpack(fmul2(f2_pack(p[c][e], p[c][e + 1]),
+                          ffma2(f2_pack(dl.x, dl.y), neg1,
+                                f2_pack(__uint_as_float(dpv[e]), __uint_as_float(dpv[e + 1])))),
+                    d0, d1);
+          f2_unpack(fmul2(f2_pack(p[c][e + 2], p[c][e + 3]),
+                          ffma2(f2_pack(dl.z, dl.w), neg1,
+                                f2_pack(__uint_as_float(dpv[e + 2]), __uint_as_float(dpv[e + 3])))),
+                    d2, d3);
+          dd[e4 * 2] = pack2<kBf16>(d0, d1);
+          dd[e4 * 2 + 1] = pack2<kBf16>(d2, d3);
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          uint4 v = make_uint4(dd[w * 4 + 0], dd[w * 4 + 1], dd[w * 4 + 2], dd[w * 4 + 3]);
+          *reinterpret_cast<uint4*>(sDS + swz_offset(t, h * 64 + c * 32 + w * 8, kTileRows)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&ld_empty[lb]);
+        mbar_arrive(ds_ready);
+      }
+    }
+    // Epilogue: WG2 stores dV (staged through Q stage 0), WG3 stores dK
+    // (scaled, staged through the dO buffer).  Rows >= S are clipped by the
+    // tensor map bounds.
+    uint8_t* stage = (h == 0) ? sQ : sDO;
+    if (ok) ok = warp_wait(dkdv_done, 0, ctl, timeout_ns, status, 15);
+    if (ok) {
+      tc_fence_after();
+      if (h == 0)
+        stage_row<D, kBf16>(t_lane + C::kColDV, stage, t, 1.0f);
+      else
+        stage_row<D, kBf16>(t_lane + C::kColDK, stage, t, scale);
+      fence_proxy_async_smem();
+    }
+    named_barrier_sync(1 + h, 128);
+    if ((warp & 3) == 0 && lane == 0 && !ctl->abort) {
+      const CUtensorMap* map = (h == 0) ? &tm_dv : &tm_dk;
+#pragma unroll
+      for (int b = 0; b < D / 64; ++b) tma_store_3d(map, stage + b * kBlockBytes, b * 64, n0, bh);
+      tma_store_commit();
+      tma_store_wait_read_all();
     }
   }
 
@@ -740,18 +631,14 @@ int launch_bwd_t(const BwdArgs& a) {
   auto kern = attn_bwd_kernel<D, kBf16, kWithDq>;
   // The setmaxnreg split inside the kernel assumes exactly kBwdLaunchRegs
   // registers per thread at launch; a build that differs is refused.
-  int sms = 0;
-  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, kBwdLaunchRegs, &sms))
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, kBwdLaunchRegs, nullptr))
     return rc;
   const int n_tiles = static_cast<int>((a.S + kTileRows - 1) / kTileRows);
-  const long long n_units = a.causal ? static_cast<long long>((n_tiles + 1) / 2) * a.BH
-                                     : static_cast<long long>(n_tiles) * a.BH;
-  if (n_units > 0x7fffffffLL) return kErrTooLarge;
-  const int grid = static_cast<int>(n_units < sms ? n_units : sms);
-  kern<<<grid, kBwdThreads, C::kSmemBytes, a.stream>>>(
-      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, kWithDq ? *a.tm_dq : *a.tm_q, static_cast<uint16_t*>(a.dk),
-      static_cast<uint16_t*>(a.dv), a.lse, a.delta, static_cast<int>(a.S), n_tiles, static_cast<int>(n_units),
-      a.causal, a.scale, a.scale_log2, static_cast<int>(a.D), a.timeout_ns, a.status);
+  const long long grid = static_cast<long long>(n_tiles) * a.BH;
+  kern<<<static_cast<unsigned>(grid), kBwdThreads, C::kSmemBytes, a.stream>>>(
+      *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_do, *a.tm_dk, *a.tm_dv, kWithDq ? *a.tm_dq : *a.tm_dk, a.lse, a.delta,
+      static_cast<int>(a.S), static_cast<int>(a.BH), n_tiles, a.causal, a.scale, a.scale_log2,
+      static_cast<int>(a.D), a.timeout_ns, a.status);
   return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 

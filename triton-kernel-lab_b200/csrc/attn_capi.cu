@@ -244,7 +244,7 @@ int tk_attn_bwd_fused(const void* q, const void* k, const void* v, const void* d
   if (int rc = make_map_f32(&mdq, dq_accum, bh, seq, head_dim)) return rc;
   tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, &mdq, lse, delta,
                 bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
-                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream), dk, dv};
+                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
   return tk::launch_attn_bwd(a);
 }
 
@@ -407,7 +407,7 @@ int tk_attn_bwd_dkdv(const void* q, const void* k, const void* v, const void* d_
   if (int rc = make_map(&mdv, dv, bh, seq, head_dim, dtype)) return rc;
   tk::BwdArgs a{&mq,  &mk,   &mv,      &mdo,       &mdk,   &mdv, nullptr, lse, delta,
                 bh,   seq,   head_dim, dtype == TK_DTYPE_BF16, causal ? 1 : 0, scale,
-                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream), dk, dv};
+                scale * kLog2e, g_timeout_ns, status, static_cast<cudaStream_t>(stream)};
   return tk::launch_attn_bwd_dkdv(a);
 }
 

@@ -75,10 +75,6 @@ struct BwdArgs {
   unsigned long long timeout_ns;
   int* status;
   cudaStream_t stream;
-  // dK and dV outputs, (B*H, S, D) 16-bit, stored row by row from registers.
-  // Last, so positional initialisers of the fields above stay valid.
-  void* dk = nullptr;
-  void* dv = nullptr;
 };
 
 // Backward for 128 < head_dim <= 256 (attn_bwd_d256_sm100.cu): Q and dO maps
