@@ -883,6 +883,65 @@ def run_wide(args: argparse.Namespace) -> None:
     check_device_status()
 
 
+def run_compare_sdpa(args: argparse.Namespace) -> None:
+    """Context, not a target: torch's own SDPA (cuDNN's fused attention on
+    this part) beside this library on the same inputs, 1 GPU.  For C3 and
+    C2, and the reference's registered benchmark shape (B=1, H=16, D=64,
+    fp16, S 2048 and 8192): forward and forward+backward through the public
+    autograd API of each, CUDA events around each call after an L2 flush,
+    medians of ``--steps`` calls; TFLOP/s under the reference's FLOP model.
+    One JSON line per shape."""
+    import torch.nn.functional as F
+
+    from tklab.kernels.flash_attention import attention_causal, attention_noncausal, check_device_status
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    shapes = [("c3", CONFIGS["c3"]), ("c2", CONFIGS["c2"]),
+              ("registered S=2048", (1, 16, 2048, 64, torch.float16, True, 1.0)),
+              ("registered S=8192", (1, 16, 8192, 64, torch.float16, False, 1.0))]
+    for name, (b, h, s, d, dtype, causal, qk_std) in shapes:
+        q, k, v, do = _make_inputs((b, h, s, d), dtype, qk_std, args.seed, device)
+        ours = attention_causal if causal else attention_noncausal
+
+        def sdpa(x, y, z):
+            return F.scaled_dot_product_attention(x, y, z, is_causal=causal)
+
+        row = {"compare_sdpa": name, "B": b, "H": h, "S": s, "D": d, "causal": causal,
+               "dtype": str(dtype).replace("torch.", "")}
+        for label, fn in (("ours", ours), ("torch_sdpa", sdpa)):
+            for mode in ("fwd", "fwd_bwd"):
+                def call() -> None:
+                    if mode == "fwd":
+                        with torch.no_grad():
+                            fn(q, k, v)
+                    else:
+                        qg, kg, vg = (t.detach().requires_grad_(True) for t in (q, k, v))
+                        out = fn(qg, kg, vg)
+                        torch.autograd.grad(out, (qg, kg, vg), grad_outputs=do)
+
+                for _ in range(args.warmup):
+                    call()
+                samples = []
+                for _ in range(args.steps):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    call()
+                    e1.record()
+                    torch.cuda.synchronize(device)
+                    samples.append(e0.elapsed_time(e1))
+                ms = statistics.median(samples)
+                flops = fwd_flops(b, h, s, d, causal) + (bwd_flops(b, h, s, d, causal) if mode == "fwd_bwd" else 0)
+                row[f"{label}_{mode}_ms"] = round(ms, 4)
+                row[f"{label}_{mode}_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+        row["sdpa_backend_note"] = "torch F.scaled_dot_product_attention (cuDNN fused attention on B200)"
+        print(json.dumps(row), flush=True)
+        del q, k, v, do
+    check_device_status()
+
+
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--gpus", type=int, default=1)
@@ -907,6 +966,8 @@ def main() -> None:
                         help="fused RoPE attention vs plain and unfused, one JSON line per measurement (1 GPU)")
     parser.add_argument("--wide", action="store_true",
                         help="forward for head_dim 192/256 (the 256-column kernel), one JSON line per shape (1 GPU)")
+    parser.add_argument("--compare-sdpa", action="store_true",
+                        help="torch SDPA (cuDNN) beside this library at C3, C2 and the registered shape (1 GPU)")
     parser.add_argument("--shape", type=lambda t: [int(x) for x in t.split(",")], default=None,
                         help="one shape instead of the mode's list: --wide B,H,S,D (causal); --decode B,Hq,Hkv,Dh,L")
     args = parser.parse_args()
@@ -920,6 +981,8 @@ def main() -> None:
         run_decode(args)
     elif args.wide:
         run_wide(args)
+    elif args.compare_sdpa:
+        run_compare_sdpa(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
