@@ -30,5 +30,7 @@ def max_relative_offset(tensor: torch.Tensor) -> int:
 
 def assert_int32_addressable(tensor: torch.Tensor, *, name: str) -> None:
     """Raise ``ValueError`` when ``tensor`` spans more than ``MAX_INT32_OFFSET``."""
-    if max_relative_offset(tensor) > MAX_INT32_OFFSET:
+    # A contiguous tensor's largest displacement is numel - 1 (the same sum).
+    reach = tensor.numel() - 1 if tensor.is_contiguous() and tensor.numel() > 0 else max_relative_offset(tensor)
+    if reach > MAX_INT32_OFFSET:
         raise ValueError(f"{name} strides exceed the signed int32 offset range")

@@ -125,6 +125,28 @@ def _stream(tensor: torch.Tensor) -> int:
     return int(torch.cuda.current_stream(tensor.device).cuda_stream)
 
 
+class _on_device:
+    """``torch.cuda.device(dev)`` only when ``dev`` is not already current.
+
+    The C ABI launches on the current CUDA device; switching (and switching
+    back) costs a few microseconds of host time per call, which at small
+    shapes is a visible share of the whole call.
+    """
+
+    __slots__ = ("_ctx",)
+
+    def __init__(self, device: torch.device) -> None:
+        self._ctx = None if device.index == torch.cuda.current_device() else torch.cuda.device(device)
+
+    def __enter__(self) -> None:
+        if self._ctx is not None:
+            self._ctx.__enter__()
+
+    def __exit__(self, *exc: object) -> None:
+        if self._ctx is not None:
+            self._ctx.__exit__(*exc)
+
+
 def check_device_status(device: torch.device | int | None = None) -> None:
     """Synchronise the current stream of ``device`` and raise if a kernel
     reported a device-side error (a bounded wait that ran out)."""
@@ -161,6 +183,20 @@ def _launch_forward(
     placeholder, exactly as in the reference launcher (``:296-347``).
     """
     _validate(q, k, v)
+    _forward_checked(q, k, v, output, softmax_lse, causal=causal, store_lse=store_lse)
+
+
+def _forward_checked(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    output: torch.Tensor,
+    softmax_lse: torch.Tensor,
+    *,
+    causal: bool,
+    store_lse: bool,
+) -> None:
+    """``_launch_forward`` after ``_validate(q, k, v)`` has passed (the buffers are still checked)."""
     if output.shape != q.shape or output.device != q.device or output.dtype != q.dtype:
         raise ValueError("attention output metadata must match Q")
     if not output.is_contiguous():
@@ -178,7 +214,7 @@ def _launch_forward(
         assert_int32_addressable(softmax_lse, name="log-sum-exp buffer")
         lse_ptr = softmax_lse.data_ptr()
     lib = _native.load()
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         status = lib.tk_attn_fwd(
             q.data_ptr(),
             k.data_ptr(),
@@ -242,6 +278,21 @@ def _launch_backward(
     if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
         raise ValueError("attention upstream gradient metadata must match Q")
     _validate(q, k, v, max_head_dim=MAX_HEAD_DIM)
+    return _backward_checked(q, k, v, output, softmax_lse, do, causal=causal, deterministic=deterministic)
+
+
+def _backward_checked(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    output: torch.Tensor,
+    softmax_lse: torch.Tensor,
+    do: torch.Tensor,
+    *,
+    causal: bool,
+    deterministic: bool | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """``_launch_backward`` after ``do``'s metadata and ``_validate(q, k, v)`` have passed."""
     do = do.contiguous()
     batch, heads, n_ctx, head_dim = q.shape
     if (
@@ -262,14 +313,18 @@ def _launch_backward(
             deterministic = False
         else:
             raise RuntimeError(message)
-    delta = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
+    # delta and (default path) the fp32 dQ accumulator share one allocation:
+    # the accumulator first (16-byte aligned), delta after it.
+    n_acc = 0 if deterministic else batch * heads * n_ctx * head_dim
+    workspace = torch.empty(n_acc + batch * heads * n_ctx, dtype=torch.float32, device=q.device)
+    delta = workspace[n_acc:].view(batch, heads, n_ctx)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     lib = _native.load()
     dtype = _NATIVE_DTYPE[q.dtype]
     if deterministic:
-        with torch.cuda.device(q.device):
+        with _on_device(q.device):
             status = lib.tk_attn_bwd_deterministic(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), output.data_ptr(), do.data_ptr(),
                 softmax_lse.data_ptr(), delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
@@ -278,8 +333,8 @@ def _launch_backward(
             _native.check(status, "tk_attn_bwd_deterministic")
         _after_launch(q.device)
         return dq, dk, dv
-    dq_accum = torch.empty((batch, heads, n_ctx, head_dim), dtype=torch.float32, device=q.device)
-    with torch.cuda.device(q.device):
+    dq_accum = workspace[:n_acc].view(batch, heads, n_ctx, head_dim)
+    with _on_device(q.device):
         stream = _stream(q)
         status = lib.tk_attn_bwd_pre(
             output.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
@@ -309,12 +364,14 @@ class _FlashAttentionFunction(torch.autograd.Function):
         v: torch.Tensor,
         causal: bool,
     ) -> torch.Tensor:
-        """Run the forward kernel with the statistic stored for the backward."""
-        _validate(q, k, v)
+        """Run the forward kernel with the statistic stored for the backward.
+
+        Q, K and V were validated by ``_attention`` (the only caller).
+        """
         output = torch.empty_like(q)
         batch, heads, n_ctx, _ = q.shape
         softmax_lse = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
-        _launch_forward(q, k, v, output, softmax_lse, causal=causal, store_lse=True)
+        _forward_checked(q, k, v, output, softmax_lse, causal=causal, store_lse=True)
         ctx.save_for_backward(q, k, v, output, softmax_lse)
         ctx.causal = causal
         return output
@@ -327,7 +384,10 @@ class _FlashAttentionFunction(torch.autograd.Function):
     ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, None]:
         """Compute Q, K and V gradients with the recompute backward."""
         q, k, v, output, softmax_lse = ctx.saved_tensors
-        dq, dk, dv = _launch_backward(q, k, v, output, softmax_lse, do, causal=ctx.causal)
+        if do.shape != q.shape or do.device != q.device or do.dtype != q.dtype:
+            raise ValueError("attention upstream gradient metadata must match Q")
+        # Q, K and V passed _validate in the forward and are unchanged.
+        dq, dk, dv = _backward_checked(q, k, v, output, softmax_lse, do, causal=ctx.causal)
         return dq, dk, dv, None
 
 
@@ -343,7 +403,7 @@ def _attention(
     needs_grad = torch.is_grad_enabled() and any(tensor.requires_grad for tensor in (q, k, v))
     if not needs_grad:
         output = torch.empty_like(q)
-        _launch_forward(q, k, v, output, output, causal=causal, store_lse=False)
+        _forward_checked(q, k, v, output, output, causal=causal, store_lse=False)
         return output
     result = _FlashAttentionFunction.apply(q, k, v, causal)
     return cast(torch.Tensor, result)
