@@ -334,8 +334,10 @@ int tk_gqa_decode(const void* q, const void* k, const void* v, const int32_t* kv
   if (int rc = status_ptr(&status)) return rc;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
-    return tk::kErrLaunch;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+    cudaGetLastError();  // do not leave the error for the next launch check
+    return tk::kErrNoDriver;
+  }
   const bool use_tc = g_decode_path != 0 && tk::gqa_decode_tc_supported(head_dim, group) &&
                       batch * q_heads <= INT_MAX;
   const int splits = use_tc ? tk::gqa_decode_splits_tc(batch, kv_heads, seq_kv, head_dim, sms)

@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 
 from tklab import _native
-from tklab.kernels.flash_attention import _NATIVE_DTYPE, _after_launch, _stream
+from tklab.kernels.flash_attention import _NATIVE_DTYPE, _after_launch, _on_device, _stream
 
 DECODE_GROUPS = (1, 2, 4, 8, 16)
 DECODE_HEAD_DIMS = (64, 128)
@@ -159,7 +159,7 @@ def gqa_decode(
     lse = torch.empty((batch, q_heads), dtype=torch.float32, device=q.device) if return_lse else None
     ws_bytes = int(lib.tk_gqa_decode_workspace_bytes(batch, q_heads, seq_kv, head_dim))
     workspace = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=q.device)
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         status = lib.tk_gqa_decode(
             q3.data_ptr(), k.data_ptr(), v.data_ptr(), None if kv_lens is None else kv_lens.data_ptr(),
             out.data_ptr(), None if lse is None else lse.data_ptr(), workspace.data_ptr(), ws_bytes,

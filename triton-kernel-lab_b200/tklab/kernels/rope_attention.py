@@ -47,6 +47,7 @@ from tklab.kernels.flash_attention import (
     _after_launch,
     _flops_factory,
     _metadata_factory,
+    _on_device,
     _stream,
     _validate,
 )
@@ -99,7 +100,7 @@ def _launch_forward_rope(
     if k_rot.shape != k.shape or k_rot.dtype != k.dtype or not k_rot.is_contiguous():
         raise ValueError("rotated-K workspace metadata must match K")
     lib = _native.load()
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         status = lib.tk_attn_fwd_rope(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), cos32.data_ptr(), sin32.data_ptr(), k_rot.data_ptr(),
             output.data_ptr(), None if softmax_lse is None else softmax_lse.data_ptr(),
@@ -118,7 +119,7 @@ def rotate(
     batch, heads, n_ctx, head_dim = x.shape
     result = torch.empty_like(x) if out is None else out
     lib = _native.load()
-    with torch.cuda.device(x.device):
+    with _on_device(x.device):
         status = lib.tk_rope_rotate(
             x.data_ptr(), result.data_ptr(), cos32.data_ptr(), sin32.data_ptr(),
             batch, heads, n_ctx, head_dim, _NATIVE_DTYPE[x.dtype], int(transpose), _stream(x),
@@ -157,7 +158,7 @@ def _launch_backward_rope(
     dv = torch.empty_like(v)
     dtype = _NATIVE_DTYPE[q.dtype]
     lib = _native.load()
-    with torch.cuda.device(q.device):
+    with _on_device(q.device):
         stream = _stream(q)
         status = lib.tk_attn_bwd_pre(
             output.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
