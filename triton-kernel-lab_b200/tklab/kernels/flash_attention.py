@@ -121,7 +121,16 @@ def _validate(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, max_head_dim
         assert_int32_addressable(tensor, name=name)
 
 
+# torch's raw current-stream query (the handle Triton's launcher also uses)
+# costs well under a microsecond; building a torch.cuda.Stream object for
+# the same handle costs a few.
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(tensor: torch.Tensor) -> int:
+    """The current CUDA stream of ``tensor``'s device, as a raw handle."""
+    if _RAW_STREAM is not None:
+        return int(_RAW_STREAM(tensor.device.index))
     return int(torch.cuda.current_stream(tensor.device).cuda_stream)
 
 
@@ -314,10 +323,13 @@ def _backward_checked(
         else:
             raise RuntimeError(message)
     # delta and (default path) the fp32 dQ accumulator share one allocation:
-    # the accumulator first (16-byte aligned), delta after it.
+    # the accumulator first (16-byte aligned), delta after it (4 * n_acc
+    # bytes in, a multiple of 32 because head_dim is a multiple of 8).  The
+    # kernels take raw pointers, so no views are built.
     n_acc = 0 if deterministic else batch * heads * n_ctx * head_dim
     workspace = torch.empty(n_acc + batch * heads * n_ctx, dtype=torch.float32, device=q.device)
-    delta = workspace[n_acc:].view(batch, heads, n_ctx)
+    dq_accum_ptr = workspace.data_ptr()
+    delta_ptr = dq_accum_ptr + 4 * n_acc
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
@@ -327,23 +339,22 @@ def _backward_checked(
         with _on_device(q.device):
             status = lib.tk_attn_bwd_deterministic(
                 q.data_ptr(), k.data_ptr(), v.data_ptr(), output.data_ptr(), do.data_ptr(),
-                softmax_lse.data_ptr(), delta.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                softmax_lse.data_ptr(), delta_ptr, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
                 batch, heads, n_ctx, head_dim, dtype, int(bool(causal)), 1.0 / math.sqrt(head_dim), _stream(q),
             )
             _native.check(status, "tk_attn_bwd_deterministic")
         _after_launch(q.device)
         return dq, dk, dv
-    dq_accum = workspace[:n_acc].view(batch, heads, n_ctx, head_dim)
     with _on_device(q.device):
         stream = _stream(q)
         status = lib.tk_attn_bwd_pre(
-            output.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+            output.data_ptr(), do.data_ptr(), delta_ptr, dq_accum_ptr,
             batch, heads, n_ctx, head_dim, dtype, stream,
         )
         _native.check(status, "tk_attn_bwd_pre")
         status = lib.tk_attn_bwd(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), do.data_ptr(),
-            softmax_lse.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
+            softmax_lse.data_ptr(), delta_ptr, dq_accum_ptr,
             dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
             batch, heads, n_ctx, head_dim, dtype, int(bool(causal)),
             1.0 / math.sqrt(head_dim), stream,
