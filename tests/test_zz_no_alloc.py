@@ -7,8 +7,10 @@ pool owns every device byte, an allocation-free hot loop — so they cannot hand
 scratch in a 64 MiB array inside the library instead.  This file checks,
 through the C ABI, that two calls in a row (different inputs, so the second
 one depends on the shared scratch being re-cleared) give the same dQ, dK and
-dV as the regular entry points, and that an over-capacity problem is refused
-before anything is launched.  It sits in its own file, collected last.
+dV as the regular entry points and as the CPU fp32 oracle
+(``oracle.attention_oracle.manual_backward``), and that an over-capacity
+problem is refused before anything is launched.  It sits in its own file,
+collected last.
 """
 
 from __future__ import annotations
@@ -18,6 +20,7 @@ import math
 import pytest
 import torch
 
+from oracle.attention_oracle import manual_backward
 from tklab import _native
 from tklab.harness.tolerances import relative_frobenius_error
 from tklab.kernels.flash_attention import _NATIVE_DTYPE, _launch_forward, check_device_status
@@ -76,11 +79,16 @@ def test_noalloc_backward_matches_regular_entry_point_twice(shape, dtype, causal
         expected = _regular(lib, q, k, v, o, do, lse, causal, stream)
         got = _noalloc(lib, q, k, v, o, do, lse, causal, stream)
         check_device_status()
-        for name, g, e in zip(("dq", "dk", "dv"), got, expected, strict=True):
+        oracle = manual_backward(q, k, v, do, causal=causal)
+        for name, g, e, r in zip(("dq", "dk", "dv"), got, expected, oracle, strict=True):
             g, e = g.float().cpu(), e.float().cpu()
             assert torch.isfinite(g).all(), (call, name)
             assert (g - e).abs().max().item() <= 5e-2, (call, name)
             assert relative_frobenius_error(g, e) < 2e-2, (call, name)
+            # Against the CPU fp32 oracle: the gradient tolerances of the
+            # parity tests (max abs 5e-2, relative Frobenius 2e-2).
+            assert (g - r).abs().max().item() <= 5e-2, (call, name, "oracle")
+            assert relative_frobenius_error(g, r) < 2e-2, (call, name, "oracle")
 
 
 def test_noalloc_refuses_problems_beyond_its_scratch() -> None:

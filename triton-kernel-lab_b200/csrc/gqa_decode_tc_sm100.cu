@@ -395,7 +395,6 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
       tmem_ld16(t_lane + kColO, o);
       tmem_wait_ld();
       reg_fence16(o);
-#pragma unroll
       if (t < D)
 #pragma unroll
         for (int g = 0; g < G; ++g) part_o[(part0 + static_cast<size_t>(g) * n_splits) * D + t] = __uint_as_float(o[g]);
@@ -409,7 +408,6 @@ __global__ void __launch_bounds__(kTcThreads, TcCfg<D>::kMinBlocks)
       }
     } else {
       // No keys in this split, or a wait that ran out: a neutral partial.
-#pragma unroll
       if (t < D)
 #pragma unroll
         for (int g = 0; g < G; ++g) part_o[(part0 + static_cast<size_t>(g) * n_splits) * D + t] = 0.0f;
