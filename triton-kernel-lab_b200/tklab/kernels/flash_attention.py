@@ -222,6 +222,25 @@ def _forward_checked(
             raise ValueError("attention log-sum-exp buffer must be contiguous float32 BxHxN")
         assert_int32_addressable(softmax_lse, name="log-sum-exp buffer")
         lse_ptr = softmax_lse.data_ptr()
+    _forward_launch(q, k, v, output, lse_ptr, causal=causal)
+
+
+def _forward_launch(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    output: torch.Tensor,
+    lse_ptr: int | None,
+    *,
+    causal: bool,
+) -> None:
+    """The library call itself, for a validated Q/K/V and buffers whose metadata is known to match.
+
+    ``_forward_checked`` reaches it after checking caller-supplied buffers;
+    ``_attention`` and the autograd forward call it directly with buffers
+    they allocated themselves (``empty_like(q)`` and a float32 BxHxN LSE).
+    """
+    batch, heads, n_ctx, head_dim = q.shape
     lib = _native.load()
     with _on_device(q.device):
         status = lib.tk_attn_fwd(
@@ -382,7 +401,7 @@ class _FlashAttentionFunction(torch.autograd.Function):
         output = torch.empty_like(q)
         batch, heads, n_ctx, _ = q.shape
         softmax_lse = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
-        _forward_checked(q, k, v, output, softmax_lse, causal=causal, store_lse=True)
+        _forward_launch(q, k, v, output, softmax_lse.data_ptr(), causal=causal)
         ctx.save_for_backward(q, k, v, output, softmax_lse)
         ctx.causal = causal
         return output
@@ -414,7 +433,7 @@ def _attention(
     needs_grad = torch.is_grad_enabled() and any(tensor.requires_grad for tensor in (q, k, v))
     if not needs_grad:
         output = torch.empty_like(q)
-        _forward_checked(q, k, v, output, output, causal=causal, store_lse=False)
+        _forward_launch(q, k, v, output, None, causal=causal)
         return output
     result = _FlashAttentionFunction.apply(q, k, v, causal)
     return cast(torch.Tensor, result)
