@@ -13,9 +13,10 @@
 //
 // A work item is two consecutive 128-row query tiles (A and B) of one
 // (batch, head); the CTA streams the key/value tiles once for both.  Large
-// causal problems run one persistent CTA per SM over balanced units of items
-// (the next item's Q load and first products overlap the current epilogue);
-// otherwise one CTA runs one item.  12 warps in three warpgroups, registers
+// causal problems and short non-causal ones (at most four key tiles) run one
+// persistent CTA per SM over balanced units of items (the next item's Q load
+// and first products overlap the current epilogue); otherwise one CTA runs
+// one item.  12 warps in three warpgroups, registers
 // rebalanced with setmaxnreg:
 //   WG0  warp 0   TMA producer (Q_A and Q_B per item, then K and V tiles
 //                 through two rings)
@@ -23,8 +24,10 @@
 //                 loop converged, one elected lane issues)
 //   WG1  warps 4..7   softmax of tile A: thread t owns query row t (TMEM
 //                     lane t); also rescales O_A when its running maximum
-//                     moves, and runs tile A's epilogue (O_A / row_sum stored
-//                     from registers straight to global memory)
+//                     moves, and runs tile A's epilogue (O_A / row_sum
+//                     stored from registers straight to global memory by
+//                     persistent CTAs, staged through Q_A for one TMA store
+//                     otherwise)
 //   WG2  warps 8..11  the same for tile B
 // Tensor memory (512 columns): O_A, O_B (D columns each), then S_A and S_B
 // (128 columns each).  P is written back as packed 16-bit pairs over the
