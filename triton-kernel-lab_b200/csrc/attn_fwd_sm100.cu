@@ -11,13 +11,17 @@
 // for the P.V product, O = acc / row_sum, and the optional statistic is the
 // base-2 log-sum-exp `row_max + log2(row_sum)` (:254-264).
 //
-// A work item is two consecutive 128-row query tiles (A and B) of one
-// (batch, head); the CTA streams the key/value tiles once for both.  Large
-// causal problems and short non-causal ones (at most four key tiles) run one
-// persistent CTA per SM over balanced units of items (the next item's Q load
-// and first products overlap the current epilogue); otherwise one CTA runs
-// one item.  12 warps in three warpgroups, registers
-// rebalanced with setmaxnreg:
+// At head_dim 128 a work item is two consecutive 128-row query tiles (A and
+// B) of one (batch, head); the CTA streams the key/value tiles once for both,
+// 12 warps, one CTA per SM.  At head_dim 64 an item is one query tile (A
+// only): 8 warps, 256 tensor-memory columns and 80 KB of shared memory, so
+// two CTAs share an SM and each tile's S -> softmax -> P.V chain runs on its
+// own MMA warp instead of taking turns with a second tile on one (the same
+// math per row; 2-21 % faster at head_dim 64 than two tiles per CTA).  Large
+// causal problems and short ones run persistent CTAs (one or two per SM)
+// over balanced units of items (the next item's Q load and first products
+// overlap the current epilogue); otherwise one CTA runs one item.  Warpgroups,
+// registers rebalanced with setmaxnreg:
 //   WG0  warp 0   TMA producer (Q_A and Q_B per item, then K and V tiles
 //                 through two rings)
 //        warp 1   TMEM allocator and tcgen05.mma issuer (the warp runs the
@@ -28,9 +32,9 @@
 //                     stored from registers straight to global memory by
 //                     persistent CTAs, staged through Q_A for one TMA store
 //                     otherwise)
-//   WG2  warps 8..11  the same for tile B
-// Tensor memory (512 columns): O_A, O_B (D columns each), then S_A and S_B
-// (128 columns each).  P is written back as packed 16-bit pairs over the
+//   WG2  warps 8..11  the same for tile B (head_dim 128 only)
+// Tensor memory: O_A, O_B (D columns each), then S_A and S_B (128 columns
+// each); at head_dim 64 O_A and S_A in 256 columns.  P is written back as packed 16-bit pairs over the
 // first 64 columns of its tile's S and consumed from TMEM by the P.V MMA.
 // MMA issue order per key tile j: PV_A(j), S_A(j+1), PV_B(j), S_B(j+1), so
 // while the softmax of one tile runs the tensor core works on the other
@@ -45,10 +49,22 @@ namespace {
 
 template <int D>
 struct FwdCfg {
-  static constexpr int kStages = (D == 64) ? 4 : 2;
+  // Query tiles per CTA (and softmax warpgroups), CTAs per SM.
+  static constexpr int kT = (D == 64) ? 1 : 2;
+  static constexpr int kMinBlocks = (kT == 1) ? 2 : 1;
+  static constexpr int kThreads = 128 * (1 + kT);
+  // Launch allocation kLaunchRegs x kThreads; after setmaxnreg the control
+  // warpgroup keeps 56 and each softmax warpgroup gets kRegsSoftmax
+  // (56 + kT x kRegsSoftmax = (1 + kT) x kLaunchRegs), so the increases are
+  // always satisfiable; two 256-thread CTAs x 128 registers fill an SM.
+  static constexpr int kLaunchRegs = (kT == 1) ? 128 : 168;
+  static constexpr int kRegsCtrl = 56;
+  static constexpr int kRegsSoftmax = (kT == 1) ? 200 : 224;
+  static_assert(kRegsCtrl + kT * kRegsSoftmax <= (1 + kT) * kLaunchRegs, "register split exceeds the launch");
+  static constexpr int kStages = 2;
   static constexpr int kTileBytes = kTileRows * D * 2;
-  static constexpr int kQOff = 0;  // Q_A, Q_B
-  static constexpr int kKOff = kQOff + 2 * kTileBytes;
+  static constexpr int kQOff = 0;  // Q_A (, Q_B)
+  static constexpr int kKOff = kQOff + kT * kTileBytes;
   static constexpr int kVOff = kKOff + kStages * kTileBytes;
   static constexpr int kBarOff = kVOff + kStages * kTileBytes;
   // q_full, q_empty, k_full[S], k_empty[S], v_full[S], v_empty[S],
@@ -57,20 +73,12 @@ struct FwdCfg {
   static constexpr int kNumBars = 2 + 4 * kStages + 8;
   static constexpr int kCtlOff = kBarOff + kNumBars * 8;
   static constexpr int kSmemBytes = kCtlOff + 64;
-  static constexpr uint32_t kTmemCols = 512;
-  // O of tile x at column x * D, S of tile x at 2D + 128 x.
+  static constexpr uint32_t kTmemCols = (kT == 1) ? 256 : 512;
+  // O of tile x at column x * D, S of tile x at kT D + 128 x.
   static constexpr uint32_t kColO0 = 0;
-  static constexpr uint32_t kColS0 = 2 * D;
+  static constexpr uint32_t kColS0 = kT * D;
 };
 
-constexpr int kFwdThreads = 384;
-// Launch allocation 168 registers x 384 threads; after setmaxnreg the control
-// warpgroup keeps 56 and each softmax warpgroup gets 224 (56 + 2 x 224 =
-// 3 x 168), so the increases are always satisfiable.
-constexpr int kFwdLaunchRegs = 168;
-constexpr int kFwdRegsCtrl = 56;
-constexpr int kFwdRegsSoftmax = 224;
-static_assert(kFwdRegsCtrl + 2 * kFwdRegsSoftmax <= 3 * kFwdLaunchRegs, "register split exceeds the launch");
 // The running maximum used for P is only moved when the true maximum exceeds
 // it by more than this (base-2 units), so P <= 2^8 and O is rescaled rarely.
 // The result is unchanged mathematically because O and row_sum always share
@@ -223,7 +231,7 @@ __device__ __forceinline__ void fwd_unit_item(int u, int sub, int BH, int n_ctil
 // every CTA streams every K tile, so rotating K here would repeat the work
 // once per query tile).
 template <int D, bool kBf16, bool kRope>
-__global__ void __launch_bounds__(kFwdThreads, 1)
+__global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                     uint16_t* __restrict__ out, float* __restrict__ lse, const float* __restrict__ rope_cos,
@@ -292,7 +300,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   // ...; barrier phases follow running counters (items, key tiles, S and P
   // tiles per query tile) so consecutive items pipeline into each other.
   if (wg == 0) {
-    warpgroup_reg_dec<kFwdRegsCtrl>();
+    warpgroup_reg_dec<C::kRegsCtrl>();
     if (warp == 0 && lane == 0) {
       // ---------------- TMA producer ----------------
       uint32_t g = 0;  // key tiles loaded so far
@@ -303,14 +311,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
           int bh, ct;
           fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-          const int m0 = ct * 2 * kTileRows;
-          const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
+          const int m0 = ct * C::kT * kTileRows;
+          const int n_kv_b = causal ? min(C::kT * ct + C::kT, n_ntiles) : n_ntiles;
           // Q_A and Q_B are free once the previous item's last S product
           // has completed.
           if (it > 0 && !(ok = mbar_wait(q_empty, (it - 1) & 1, ctl, timeout_ns, status, 13))) break;
-          mbar_arrive_expect_tx(q_full, 2 * C::kTileBytes);
+          mbar_arrive_expect_tx(q_full, C::kT * C::kTileBytes);
 #pragma unroll
-          for (int x = 0; x < 2; ++x)
+          for (int x = 0; x < C::kT; ++x)
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
               tma_load_3d(sQ + x * C::kTileBytes + b * kBlockBytes, &tm_q, q_full, b * 64, m0 + x * kTileRows, bh);
@@ -381,8 +389,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
           int bh, ct;
           fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-          const int n_kv_a = causal ? min(2 * ct + 1, n_ntiles) : n_ntiles;
-          const int n_kv_b = causal ? min(2 * ct + 2, n_ntiles) : n_ntiles;
+          const int n_kv_a = causal ? min(C::kT * ct + 1, n_ntiles) : n_ntiles;
+          const int n_kv_b = causal ? min(C::kT * ct + C::kT, n_ntiles) : n_ntiles;
           // S_x(0) overwrites the previous item's P_x, whose P.V was issued
           // earlier on this thread: the tensor pipe keeps that order.
           if (!(ok = warp_wait(kRope ? &q_rot[0] : q_full, it & 1, ctl, timeout_ns, status, 3))) break;
@@ -391,11 +399,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             if (!(ok = warp_wait(&k_full[st0], (g / C::kStages) & 1, ctl, timeout_ns, status, 4))) break;
             tc_fence_after();
             issue_s(0, st0);
-            if (kRope) {
-              if (!(ok = warp_wait(&q_rot[1], it & 1, ctl, timeout_ns, status, 14))) break;
-              tc_fence_after();
+            if constexpr (C::kT == 2) {
+              if (kRope) {
+                if (!(ok = warp_wait(&q_rot[1], it & 1, ctl, timeout_ns, status, 14))) break;
+                tc_fence_after();
+              }
+              issue_s(1, st0);
             }
-            issue_s(1, st0);
             commit(&k_empty[st0]);
             if (n_kv_b == 1) commit(q_empty);
           }
@@ -424,19 +434,29 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
                 commit(&o_final[0]);
               }
             }
-            if (!(ok = warp_wait(&p_ready[1], pb & 1, ctl, timeout_ns, status, 8))) break;
-            ++pb;
-            if (!v_ready && !(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
-            tc_fence_after();
-            issue_pv(1, st, j > 0);
-            commit(&v_empty[st]);
-            if (j1 < n_kv_b) {
-              if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
-              issue_s(1, st1);
-              commit(&k_empty[st1]);
-              if (j1 == n_kv_b - 1) commit(q_empty);  // the item's last S product
+            if constexpr (C::kT == 2) {
+              if (!(ok = warp_wait(&p_ready[1], pb & 1, ctl, timeout_ns, status, 8))) break;
+              ++pb;
+              if (!v_ready && !(ok = warp_wait(&v_full[st], ph, ctl, timeout_ns, status, 9))) break;
+              tc_fence_after();
+              issue_pv(1, st, j > 0);
+              commit(&v_empty[st]);
+              if (j1 < n_kv_b) {
+                if (!k_ready && !(ok = warp_wait(&k_full[st1], ph1, ctl, timeout_ns, status, 10))) break;
+                issue_s(1, st1);
+                commit(&k_empty[st1]);
+                if (j1 == n_kv_b - 1) commit(q_empty);  // the item's last S product
+              } else {
+                commit(&o_final[1]);
+              }
             } else {
-              commit(&o_final[1]);
+              // One tile (n_kv_a == n_kv_b): P_A(j).V read V_j and S_A(j+1)
+              // read K_{j+1}.
+              commit(&v_empty[st]);
+              if (j1 < n_kv_b) {
+                commit(&k_empty[st1]);
+                if (j1 == n_kv_b - 1) commit(q_empty);  // the item's last S product
+              }
             }
           }
           g += n_kv_b;
@@ -444,7 +464,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
   } else {
-    warpgroup_reg_inc<kFwdRegsSoftmax>();
+    warpgroup_reg_inc<C::kRegsSoftmax>();
     // ---------------- softmax / correction / epilogue of tile x ----------------
     const int x = wg - 1;
     const int q4 = warp & 3;
@@ -462,9 +482,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
         int bh, ct;
         fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-        const int m0 = ct * 2 * kTileRows;
+        const int m0 = ct * C::kT * kTileRows;
         const int row_g = m0 + x * kTileRows + r;
-        const int n_kv_x = causal ? min(2 * ct + 1 + x, n_ntiles) : n_ntiles;
+        const int n_kv_x = causal ? min(C::kT * ct + 1 + x, n_ntiles) : n_ntiles;
         if constexpr (kRope) {
           // Rotate this thread's row of Q_x once the item's Q has landed.
           // (No early exit: after a failed wait the warps still reach the
@@ -601,28 +621,34 @@ int launch_fwd_t(const FwdArgs& a) {
   using C = FwdCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "forward shared memory exceeds the sm_100 limit");
   auto kern = attn_fwd_kernel<D, kBf16, kRope>;
-  // The setmaxnreg split inside the kernel assumes exactly kFwdLaunchRegs
+  // The setmaxnreg split inside the kernel assumes exactly C::kLaunchRegs
   // registers per thread at launch; a build that differs is refused.
   int sms = 0;
-  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, kFwdLaunchRegs, &sms))
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, C::kLaunchRegs, &sms))
     return rc;
-  const int n_ctiles = static_cast<int>((a.S + 2 * kTileRows - 1) / (2 * kTileRows));
+  const int n_ctiles = static_cast<int>((a.S + C::kT * kTileRows - 1) / (C::kT * kTileRows));
   const long long n_items = static_cast<long long>(n_ctiles) * a.BH;
   const long long n_pair_units = static_cast<long long>((n_ctiles + 1) / 2) * a.BH;
   int mode;
   long long n_units, grid;
-  if (n_ctiles > 1 && n_pair_units >= 2LL * sms && (a.causal || a.S <= 4 * kTileRows)) {
-    // Persistent: one CTA per SM walks equal-cost paired units, so the next
-    // item's Q load and first products overlap the current epilogue; at
-    // least two units per SM keep the last round's imbalance small.
-    // Non-causal items only take this path when they are short (at most
-    // four key tiles, where a CTA's prologue and epilogue weigh most):
-    // measured 6-21 % faster at S = 384-512, and 1-11 % slower at S =
-    // 1024-8192, where the register-to-global epilogue costs more than the
-    // overlap saves.
+  // Persistent: the resident CTAs (one or two per SM) walk equal-cost paired
+  // units, so the next item's Q load and first products overlap the current
+  // epilogue; at least two units per resident CTA keep the last round's
+  // imbalance small.  Measured (interleaved A/B, bit-identical O): non-causal
+  // items only gain when they are short (at most four key tiles, where a
+  // CTA's prologue and epilogue weigh most: 6-21 % at S = 384-512, 1-11 %
+  // slower at S = 1024-8192, where the register-to-global epilogue costs
+  // more than the overlap saves); causal items at head_dim 128 at every
+  // length; causal single-tile items (head_dim 64) up to S = 2048 (7-19 %),
+  // beyond which two hardware-scheduled CTAs per SM balance better (9 % at
+  // S = 16384).
+  const long long resident = static_cast<long long>(C::kMinBlocks) * sms;
+  const bool persist_shape =
+      a.S <= 4 * kTileRows || (a.causal && (C::kT == 2 || a.S <= 16 * kTileRows));
+  if (n_ctiles > 1 && n_pair_units >= 2LL * resident && persist_shape) {
     mode = kOrderPaired;
     n_units = n_pair_units;
-    grid = sms;
+    grid = resident;
   } else {
     // One CTA per item, scheduled by the hardware.  Heaviest-first across
     // heads only pays when it cannot thrash L2: K and V of all heads
@@ -633,7 +659,7 @@ int launch_fwd_t(const FwdArgs& a) {
     grid = n_items;
   }
   if (n_units > INT32_MAX || grid > INT32_MAX) return kErrTooLarge;
-  kern<<<static_cast<unsigned>(grid), kFwdThreads, C::kSmemBytes, a.stream>>>(
+  kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, a.stream>>>(
       *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, static_cast<uint16_t*>(a.o), a.lse, a.rope_cos, a.rope_sin,
       static_cast<int>(a.S),
       static_cast<int>(a.BH), n_ctiles, a.causal, mode, static_cast<int>(n_units), static_cast<int>(a.D),

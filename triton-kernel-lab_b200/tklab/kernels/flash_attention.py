@@ -67,17 +67,21 @@ SUPPORTED_FWD_HEAD_DIMS = SUPPORTED_HEAD_DIMS
 MAX_DETERMINISTIC_HEAD_DIM = 128
 _NATIVE_DTYPE = {torch.float16: _native.TK_DTYPE_F16, torch.bfloat16: _native.TK_DTYPE_BF16}
 
-# Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile
-# (a forward CTA runs two query tiles), forward CTA = 12 warps, backward CTA
-# = 16 warps, K/V ring depth 4 (head_dim <= 64) or 2 (head_dim <= 128).
+# Tile shape of the sm_100a kernels: 128 query rows x 128 keys per MMA tile;
+# a forward CTA runs one query tile at head_dim <= 64 (8 warps, two CTAs per
+# SM) and two at head_dim <= 128 (12 warps); backward CTA = 16 warps; K/V
+# ring depth 2.
 _BLOCK_M = 128
 _BLOCK_N = 128
-_FWD_WARPS = 12
 _BWD_WARPS = 16
 
 
+def _fwd_warps(head_dim: int) -> int:
+    return 8 if head_dim <= 64 else 12
+
+
 def _fwd_stages(head_dim: int) -> int:
-    return 4 if head_dim <= 64 else 2
+    return 2
 
 
 # Set TKLAB_CHECK_DEVICE_STATUS=1 to synchronise after every launch and raise
@@ -510,7 +514,7 @@ def _metadata_factory(*, causal: bool) -> BenchmarkMetadataFn:
         return {
             "block_m": _BLOCK_M,
             "block_n": _BLOCK_N,
-            "num_warps": _FWD_WARPS,
+            "num_warps": _fwd_warps(_HEAD_DIM),
             "num_stages": _fwd_stages(_HEAD_DIM),
             "heads": _HEADS,
             "head_dim": _HEAD_DIM,
