@@ -225,6 +225,11 @@ def run_ours(args: argparse.Namespace) -> None:
     nd = _NATIVE_DTYPE[dtype]
     scale = 1.0 / math.sqrt(d)
     numel = q.numel()
+    # Scratch of the forward's key-split schedule (0 when this rank's slab
+    # count fills the device): allocated once, outside the timed region.
+    fwd_ws_bytes = int(lib.tk_attn_fwd_workspace_bytes(1, slab, s, d, nd, int(causal)))
+    fwd_ws = torch.empty(max(fwd_ws_bytes, 1), dtype=torch.uint8, device=device)
+    fwd_ws_ptr = fwd_ws.data_ptr() if fwd_ws_bytes else None
 
     def step(ev: list[torch.cuda.Event] | None) -> None:
         def mark(i: int) -> None:
@@ -232,8 +237,8 @@ def run_ours(args: argparse.Namespace) -> None:
                 ev[i].record(stream)
 
         mark(0)
-        _native.check(lib.tk_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-                                      1, slab, s, d, nd, int(causal), scale, sp), "fwd")
+        _native.check(lib.tk_attn_fwd_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+                                         1, slab, s, d, nd, int(causal), scale, fwd_ws_ptr, fwd_ws_bytes, sp), "fwd")
         mark(1)
         _native.check(lib.tk_attn_bwd_pre(o.data_ptr(), do.data_ptr(), delta.data_ptr(), dq_accum.data_ptr(),
                                           1, slab, s, d, nd, sp), "bwd_pre")
@@ -384,8 +389,9 @@ def run_ours(args: argparse.Namespace) -> None:
                     else None),
                 "traffic_source": "ncu dram bytes of one 64-slab launch scaled by slabs/rank",
             },
-            "gpu_launches": 4 * steps,
-            "gpu_launches_note": "per rank: fwd, bwd_pre, bwd_fused, dq_convert per step",
+            "gpu_launches": (5 if fwd_ws_bytes else 4) * steps,
+            "gpu_launches_note": ("per rank: fwd, " + ("fwd_combine, " if fwd_ws_bytes else "")
+                                  + "bwd_pre, bwd_fused, dq_convert per step"),
             "clocks": clocks,
             "per_rank": per_rank,
             "e2e": e2e,
@@ -587,9 +593,14 @@ def run_sweep(args: argparse.Namespace) -> None:
                     nd = _NATIVE_DTYPE[dtype]
                     scale = 1.0 / math.sqrt(d)
 
+                    ws_bytes = int(lib.tk_attn_fwd_workspace_bytes(1, slab, s, d, nd, int(causal)))
+                    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=device)
+                    ws_ptr = ws.data_ptr() if ws_bytes else None
+
                     def fwd() -> None:
-                        _native.check(lib.tk_attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                                                      lse.data_ptr(), 1, slab, s, d, nd, int(causal), scale, sp), "fwd")
+                        _native.check(lib.tk_attn_fwd_ws(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                                                         lse.data_ptr(), 1, slab, s, d, nd, int(causal), scale,
+                                                         ws_ptr, ws_bytes, sp), "fwd")
 
                     def bwd() -> None:
                         _native.check(lib.tk_attn_bwd_pre(o.data_ptr(), do.data_ptr(), delta.data_ptr(),
@@ -624,6 +635,7 @@ def run_sweep(args: argparse.Namespace) -> None:
                             "bwd_ms": round(times["bwd"], 4),
                             "fwd_tflops": round(ff / times["fwd"] / 1e9, 1),
                             "bwd_tflops": round(bf / times["bwd"] / 1e9, 1),
+                            "fwd_key_split": bool(ws_bytes),
                             "bwd_timed": "tk_attn_bwd_pre + tk_attn_bwd (fused kernel + dQ conversion)",
                             "l2": "flushed before every timed call"}), flush=True)
                     del q, k, v, do, o, lse, delta, acc, dq, dk, dv

@@ -24,6 +24,12 @@
  *                        _attn_bwd_dq_kernel :469-533 launches)
  *   tk_attn_bwd_fused / tk_attn_dq_convert
  *                       the two launches of tk_attn_bwd, exposed separately
+ *   tk_attn_fwd_ws / tk_attn_fwd_workspace_bytes
+ *                       _launch_forward (src/tklab/kernels/flash_attention.py:
+ *                       296-347) with optional scratch for a key-split
+ *                       schedule of problems with too few query tiles to
+ *                       fill the device; the reference launches one program
+ *                       per query tile and has no such schedule
  *   tk_attn_bwd_workspace_bytes
  *                       the fp32 dQ accumulator size; the reference needs
  *                       no workspace because its dQ pass recomputes P
@@ -71,6 +77,27 @@ extern "C" {
 TK_API int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
                 void* stream);
+
+/* Bytes of scratch tk_attn_fwd_ws can use for this problem on the current
+ * device: nonzero when the problem has too few work items for the device's
+ * SMs and its longest item would set the time (few (batch, head) slabs,
+ * long sequences; head_dim up to 128).  Such problems are then run as
+ * chunks of the key range, whose fp32 partial outputs and log-sum-exps are
+ * written to the scratch and merged by a second kernel.  0: tk_attn_fwd_ws
+ * runs exactly tk_attn_fwd.  Returns 0 for invalid arguments too. */
+TK_API size_t tk_attn_fwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                          int dtype, int causal);
+
+/* tk_attn_fwd with scratch for the key-split schedule.  workspace NULL (or
+ * workspace_bytes 0): identical to tk_attn_fwd.  Otherwise workspace must
+ * be 256-byte aligned device memory of at least
+ * tk_attn_fwd_workspace_bytes(...) bytes (TK_ERR_INVALID_ARGUMENT if
+ * smaller, TK_ERR_MISALIGNED if unaligned), private to this call until it
+ * completes on `stream`.  The result agrees with tk_attn_fwd's within
+ * fp32 rounding before the final rounding to the 16-bit output. */
+TK_API int tk_attn_fwd_ws(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
+                          int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
 /* Backward preprocessing: delta[b,h,m] = sum_d o[b,h,m,d] * d_o[b,h,m,d]
  * (fp32), and, when dq_accum is not NULL, the fp32 dQ accumulator

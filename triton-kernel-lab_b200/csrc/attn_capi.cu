@@ -164,11 +164,31 @@ extern "C" {
 int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
                 int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
                 void* stream) {
+  return tk_attn_fwd_ws(q, k, v, o, lse, batch, heads, seq, head_dim, dtype, causal, scale, nullptr, 0, stream);
+}
+
+size_t tk_attn_fwd_workspace_bytes(int64_t batch, int64_t heads, int64_t seq, int64_t head_dim, int dtype,
+                                   int causal) {
+  if (check_shape(batch, heads, seq, head_dim, dtype, 256) != tk::kOk || head_dim > 128) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return tk::attn_fwd_split_bytes(batch * heads, seq, head_dim, causal ? 1 : 0, sms);
+}
+
+int tk_attn_fwd_ws(const void* q, const void* k, const void* v, void* o, float* lse, int64_t batch,
+                   int64_t heads, int64_t seq, int64_t head_dim, int dtype, int causal, float scale,
+                   void* workspace, size_t workspace_bytes, void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || o == nullptr) return tk::kErrInvalidArgument;
   if (int rc = check_shape(batch, heads, seq, head_dim, dtype, 256)) return rc;
   if (!std::isfinite(scale) || scale <= 0.0f) return tk::kErrInvalidArgument;
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return tk::kErrMisaligned;
   if (lse != nullptr && (reinterpret_cast<uintptr_t>(lse) & 3u)) return tk::kErrMisaligned;
+  if (workspace == nullptr) workspace_bytes = 0;
+  if (workspace_bytes > 0 && (reinterpret_cast<uintptr_t>(workspace) & 255u)) return tk::kErrMisaligned;
   int* status = nullptr;
   if (int rc = status_ptr(&status)) return rc;
   const int64_t bh = batch * heads;
@@ -189,6 +209,8 @@ int tk_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse
   tk::FwdArgs a{&mq, &mk, &mv, &mo, o, lse, bh, seq, head_dim, dtype == TK_DTYPE_BF16,
                 causal ? 1 : 0, scale * kLog2e, g_timeout_ns, status,
                 static_cast<cudaStream_t>(stream)};
+  a.workspace = workspace_bytes > 0 ? workspace : nullptr;
+  a.workspace_bytes = workspace_bytes;
   return tk::launch_attn_fwd(a);
 }
 

@@ -40,6 +40,12 @@
 // while the softmax of one tile runs the tensor core works on the other
 // tile.  S_X(j+1) is issued after PV_X(j), so once a softmax warpgroup sees
 // S_X(j+1) complete it may rescale O_X without a separate barrier.
+// Problems with too few items to fill the device, whose longest item would
+// set the kernel's time, may run in the key-split mode (kOrderSplit below,
+// with a caller workspace): chunks of an item's key range in separate CTAs,
+// merged by attn_fwd_combine_kernel.
+#include <algorithm>
+
 #include "attn_launch.h"
 #include "rope_sm100.cuh"
 #include "sm100_primitives.cuh"
@@ -196,11 +202,21 @@ __device__ __forceinline__ void softmax_tile(uint32_t s_addr, int lim, float sca
 //                ct = p, so every causal unit costs the same number of key
 //                tiles and a static stride over units keeps persistent CTAs
 //                balanced.
+//   kOrderSplit  (few, long items: the longest would set the kernel's time)
+//                unit = one chunk of at most split_l key tiles of one item,
+//                enumerated chunk level by chunk level (every item's chunk 0,
+//                then chunk 1 of the items that have one, ...), heaviest
+//                query tiles first within a head.  Items with more than one
+//                chunk write O / row_sum of each chunk in fp32 and its base-2
+//                log-sum-exp to a workspace; attn_fwd_combine_kernel merges
+//                them.  The last chunk of an item also carries tile B's extra
+//                (diagonal) key tile, so every chunk has work for both tiles.
 // The launcher runs one CTA per unit (hardware scheduling) in the first two
-// modes and one persistent CTA per SM in the third.
+// modes and the split mode, and one persistent CTA per SM in the third.
 constexpr int kOrderHead = 0;
 constexpr int kOrderLpt = 1;
 constexpr int kOrderPaired = 2;
+constexpr int kOrderSplit = 3;
 
 __device__ __forceinline__ int fwd_unit_items(int u, int n_ctiles, int mode) {
   if (mode != kOrderPaired) return 1;
@@ -223,6 +239,71 @@ __device__ __forceinline__ void fwd_unit_item(int u, int sub, int BH, int n_ctil
   }
 }
 
+// First query-tile group with a chunk `c` (key tiles [c L, c L + L)) under a
+// causal mask, for kT query tiles per group: tile A of group ct sees
+// kT ct + 1 key tiles.  Shared by the launcher's unit count and the kernel's
+// decode so that both enumerate the same units.
+__host__ __device__ __forceinline__ int split_ct_min(int c, int split_l, int kT, int causal) {
+  return (!causal || c == 0) ? 0 : (c * split_l - 1) / kT + 1;
+}
+
+// One item as a role sees it: slab, query-tile group, first key tile and the
+// number of key tiles of tile A / tile B from there.
+struct FwdItem {
+  int bh, ct, j0, n_a, n_b, chunk;
+  bool split;  // one of several chunks: partial result to the workspace
+};
+
+// Chunk-level walk of the split schedule: unit u -> (bh, ct, chunk).  Run
+// once per CTA (one unit per CTA in that mode), by one thread.
+__device__ __forceinline__ void fwd_split_decode(int u, int BH, int n_ctiles, int causal, int kT, int split_l,
+                                                 int* out) {
+  int rem = u, c = 0;
+  // The launcher counts exactly the units this walk enumerates; the bound
+  // only guards the loop.
+  for (; c < 64; ++c) {
+    const int per = n_ctiles - split_ct_min(c, split_l, kT, causal);
+    if (per <= 0 || rem < BH * per) break;
+    rem -= BH * per;
+  }
+  const int per = max(n_ctiles - split_ct_min(c, split_l, kT, causal), 1);
+  out[0] = rem / per;
+  out[1] = n_ctiles - 1 - rem % per;
+  out[2] = c;
+}
+
+// split_item: the CTA's (bh, ct, chunk) in shared memory, decoded by
+// fwd_split_decode (split mode only).
+template <int kT>
+__device__ __forceinline__ FwdItem fwd_item(int u, int sub, int BH, int n_ctiles, int n_ntiles, int causal,
+                                            int mode, int split_l, const int* split_item) {
+  FwdItem f;
+  f.chunk = 0;
+  if (mode == kOrderSplit) {
+    f.bh = split_item[0];
+    f.ct = split_item[1];
+    f.chunk = split_item[2];
+  } else {
+    fwd_unit_item(u, sub, BH, n_ctiles, mode, f.bh, f.ct);
+  }
+  const int na = causal ? min(kT * f.ct + 1, n_ntiles) : n_ntiles;
+  const int nb = causal ? min(kT * f.ct + kT, n_ntiles) : n_ntiles;
+  if (mode == kOrderSplit) {
+    f.j0 = f.chunk * split_l;
+    const int ea = min(f.j0 + split_l, na);
+    const int eb = (ea == na) ? nb : ea;
+    f.n_a = ea - f.j0;
+    f.n_b = eb - f.j0;
+    f.split = na > split_l;
+  } else {
+    f.j0 = 0;
+    f.n_a = na;
+    f.n_b = nb;
+    f.split = false;
+  }
+  return f;
+}
+
 // kRope: rotate-half RoPE (tables rope_cos / rope_sin, (S, D/2) fp32) is
 // applied to each item's Q tiles in shared memory after their TMA load and
 // before the S products read them, by the softmax warpgroups (thread r
@@ -237,7 +318,8 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
                     uint16_t* __restrict__ out, float* __restrict__ lse, const float* __restrict__ rope_cos,
                     const float* __restrict__ rope_sin,
                     int S, int BH, int n_ctiles, int causal, int mode, int n_units, int d_real, float scale_log2,
-                    unsigned long long timeout_ns, int* status) {
+                    unsigned long long timeout_ns, int* status, int split_l, int split_cmax,
+                    float* __restrict__ o_part, float* __restrict__ lse_part) {
   using C = FwdCfg<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   if (smem_u32(smem) & 1023u) {
@@ -264,6 +346,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
   uint64_t* o_final = p_ready + 2;          // [2]
   uint64_t* q_rot = o_final + 2;           // [2]: Q_x rotated (RoPE)
   CtaControl* ctl = reinterpret_cast<CtaControl*>(smem + C::kCtlOff);
+  int* split_item = reinterpret_cast<int*>(smem + C::kCtlOff + 16);  // [3], split mode
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -282,6 +365,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
     mbar_init(&q_rot[0], 4);  // the four warps of softmax warpgroup x
     mbar_init(&q_rot[1], 4);
     ctl->abort = 0;
+    if (mode == kOrderSplit) fwd_split_decode(blockIdx.x, BH, n_ctiles, causal, C::kT, split_l, split_item);
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -309,10 +393,10 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         const int n_sub = fwd_unit_items(u, n_ctiles, mode);
         for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
-          int bh, ct;
-          fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-          const int m0 = ct * C::kT * kTileRows;
-          const int n_kv_b = causal ? min(C::kT * ct + C::kT, n_ntiles) : n_ntiles;
+          const FwdItem f = fwd_item<C::kT>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
+          const int bh = f.bh;
+          const int m0 = f.ct * C::kT * kTileRows;
+          const int n_kv_b = f.n_b;
           // Q_A and Q_B are free once the previous item's last S product
           // has completed.
           if (it > 0 && !(ok = mbar_wait(q_empty, (it - 1) & 1, ctl, timeout_ns, status, 13))) break;
@@ -322,19 +406,21 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
               tma_load_3d(sQ + x * C::kTileBytes + b * kBlockBytes, &tm_q, q_full, b * 64, m0 + x * kTileRows, bh);
-          for (int j = 0; j < n_kv_b; ++j, ++g) {
+          // kr: first row of the key tile being loaded.
+          int kr = f.j0 * kTileRows;
+          for (int left = n_kv_b; left > 0; --left, ++g, kr += kTileRows) {
             const int st = g % C::kStages;
             const uint32_t ph = (g / C::kStages) & 1;
             if (!(ok = mbar_wait(&k_empty[st], ph ^ 1, ctl, timeout_ns, status, 1))) break;
             mbar_arrive_expect_tx(&k_full[st], C::kTileBytes);
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
-              tma_load_3d(sK + st * C::kTileBytes + b * kBlockBytes, &tm_k, &k_full[st], b * 64, j * kTileRows, bh);
+              tma_load_3d(sK + st * C::kTileBytes + b * kBlockBytes, &tm_k, &k_full[st], b * 64, kr, bh);
             if (!(ok = mbar_wait(&v_empty[st], ph ^ 1, ctl, timeout_ns, status, 2))) break;
             mbar_arrive_expect_tx(&v_full[st], C::kTileBytes);
 #pragma unroll
             for (int b = 0; b < D / 64; ++b)
-              tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, j * kTileRows, bh);
+              tma_load_3d(sV + st * C::kTileBytes + b * kBlockBytes, &tm_v, &v_full[st], b * 64, kr, bh);
           }
         }
       }
@@ -387,10 +473,10 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         const int n_sub = fwd_unit_items(u, n_ctiles, mode);
         for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
-          int bh, ct;
-          fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-          const int n_kv_a = causal ? min(C::kT * ct + 1, n_ntiles) : n_ntiles;
-          const int n_kv_b = causal ? min(C::kT * ct + C::kT, n_ntiles) : n_ntiles;
+          // Key tiles are counted from the item's first one (f.j0).
+          const FwdItem f = fwd_item<C::kT>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
+          const int n_kv_a = f.n_a;
+          const int n_kv_b = f.n_b;
           // S_x(0) overwrites the previous item's P_x, whose P.V was issued
           // earlier on this thread: the tensor pipe keeps that order.
           if (!(ok = warp_wait(kRope ? &q_rot[0] : q_full, it & 1, ctl, timeout_ns, status, 3))) break;
@@ -480,11 +566,15 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
     for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
       const int n_sub = fwd_unit_items(u, n_ctiles, mode);
       for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
-        int bh, ct;
-        fwd_unit_item(u, sub, BH, n_ctiles, mode, bh, ct);
-        const int m0 = ct * C::kT * kTileRows;
+        int bh, m0, n_kv_x, n_first;
+        {
+          const FwdItem f = fwd_item<C::kT>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
+          bh = f.bh;
+          m0 = f.ct * C::kT * kTileRows;
+          n_kv_x = (x == 0) ? f.n_a : f.n_b;
+          n_first = f.j0 * kTileRows;  // first key of the item
+        }
         const int row_g = m0 + x * kTileRows + r;
-        const int n_kv_x = causal ? min(C::kT * ct + 1 + x, n_ntiles) : n_ntiles;
         if constexpr (kRope) {
           // Rotate this thread's row of Q_x once the item's Q has landed.
           // (No early exit: after a failed wait the warps still reach the
@@ -501,7 +591,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
         for (int j = 0; ok && j < n_kv_x; ++j, ++cs) {
           if (!(ok = warp_wait(&s_full[x], cs & 1, ctl, timeout_ns, status, 11))) break;
           tc_fence_after();
-          const int n0 = j * kTileRows;
+          const int n0 = n_first + j * kTileRows;
           int lim = S - n0;
           if (causal) lim = min(lim, row_g - n0 + 1);
           float alpha;
@@ -537,7 +627,30 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
         if (ok) tc_fence_after();
         const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
         const bool row_ok = row_g < S;
-        if (mode != kOrderPaired) {
+        // (Split state re-derived here rather than held through the key loop.)
+        const int n_kv_item_a = causal ? min(m0 / kTileRows + 1, n_ntiles) : n_ntiles;
+        const bool split_out = mode == kOrderSplit && n_kv_item_a > split_l;
+        if (split_out) {
+          // One chunk of a split item: O_x / row_sum of this chunk in fp32
+          // (all D columns; those past the true head_dim are zero) and its
+          // base-2 log-sum-exp, for attn_fwd_combine_kernel.
+          const size_t prow = (static_cast<size_t>(bh) * split_cmax + split_item[2]) * S + row_g;
+          float* orow = o_part + prow * D;
+#pragma unroll
+          for (int cb = 0; ok && cb < D / 32; ++cb) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + cb * 32, o);
+            tmem_wait_ld();
+            reg_fence(o);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * inv_l);
+            if (row_ok) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) st_global_v8(orow + cb * 32 + q * 8, &o[q * 8]);
+            }
+          }
+          if (ok && row_ok) lse_part[prow] = m_run + lg2(l_run);
+        } else if (mode != kOrderPaired) {
           // One item per CTA: O_x / row_sum staged through Q_x (dead once O_x
           // is final) and written by one TMA store, which clips rows past S
           // and columns past the true head_dim.
@@ -602,7 +715,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
             }
           }
         }
-        if (ok && lse != nullptr && row_ok) lse[static_cast<size_t>(bh) * S + row_g] = m_run + lg2(l_run);
+        if (ok && lse != nullptr && row_ok && !split_out) lse[static_cast<size_t>(bh) * S + row_g] = m_run + lg2(l_run);
       }
     }
   }
@@ -614,6 +727,133 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }
+}
+
+// Merges the chunks of split items: for a row whose item has nch > 1 chunks
+// with outputs O_c (already divided by their own row sums) and base-2
+// log-sum-exps L_c, M = max_c L_c, w_c = 2^(L_c - M),
+// O = sum_c w_c O_c / sum_c w_c and LSE = M + log2(sum_c w_c).  One warp per
+// row (lane c holds chunk c's L_c; nch <= 32); rows of single-chunk items
+// were written by the forward itself.
+template <int D, bool kBf16>
+__global__ void __launch_bounds__(256)
+    attn_fwd_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ lse_part,
+                            uint16_t* __restrict__ out, float* __restrict__ lse, int S, int row0, long long n_rows,
+                            int causal, int kT, int split_l, int split_cmax, int n_ntiles, int d_real) {
+  const long long wrow = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wrow >= n_rows) return;
+  const int rows_per = S - row0;
+  const int bh = static_cast<int>(wrow / rows_per);
+  const int m = row0 + static_cast<int>(wrow % rows_per);
+  const int ct = m / (kT * kTileRows);
+  const int na = causal ? min(kT * ct + 1, n_ntiles) : n_ntiles;
+  const int nch = (na + split_l - 1) / split_l;
+  if (nch <= 1) return;
+  const size_t base = static_cast<size_t>(bh) * split_cmax * S + m;  // chunk c at base + c S
+  const float lc = (lane < nch) ? lse_part[base + static_cast<size_t>(lane) * S] : -INFINITY;
+  float mx = lc;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const float w = (lane < nch) ? ex2(lc - mx) : 0.0f;
+  float sum = w;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  constexpr int kPer = D / 32;  // columns per lane
+  float acc[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) acc[e] = 0.0f;
+  for (int c = 0; c < nch; ++c) {
+    const float wc = __shfl_sync(0xffffffffu, w, c);
+    const float* src = o_part + (base + static_cast<size_t>(c) * S) * D + lane * kPer;
+    if constexpr (kPer == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src);
+      acc[0] += wc * v.x;
+      acc[1] += wc * v.y;
+      acc[2] += wc * v.z;
+      acc[3] += wc * v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(src);
+      acc[0] += wc * v.x;
+      acc[1] += wc * v.y;
+    }
+  }
+  const float inv = 1.0f / sum;
+  // head_dim is a multiple of 8, so a lane's columns are all inside it or all
+  // past it, and rows start on 16-byte boundaries.
+  if (lane * kPer < d_real) {
+    uint16_t* dst = out + (static_cast<size_t>(bh) * S + m) * d_real + lane * kPer;
+    if constexpr (kPer == 4) {
+      *reinterpret_cast<uint2*>(dst) = make_uint2(pack2<kBf16>(acc[0] * inv, acc[1] * inv),
+                                                  pack2<kBf16>(acc[2] * inv, acc[3] * inv));
+    } else {
+      *reinterpret_cast<uint32_t*>(dst) = pack2<kBf16>(acc[0] * inv, acc[1] * inv);
+    }
+  }
+  if (lse != nullptr && lane == 0) lse[static_cast<size_t>(bh) * S + m] = mx + lg2(sum);
+}
+
+// The key-split schedule.  Used only when the regular one would not be
+// persistent, its longest item has at least 48 key tiles and at least twice
+// the average load of a resident CTA (the device is less than half busy on
+// average while that item runs): chunks of split_l key tiles (at least 16,
+// sized so that there are about kSplitUnitsPerCta chunks' worth of tile-A
+// key tiles per resident CTA), at most 32 chunks per item.  Measured on one
+// B200 (split against unsplit, bf16, L2 flushed, interleaved): (B, H, S) =
+// (1, 2, 8192) causal 1.94x, (1, 4, 8192) causal 1.17x, (1, 2, 16384)
+// causal 1.41x (head_dim 128) and 1.34x (64), (1, 1, 16384) non-causal
+// 1.53x, (1, 1, 32768) causal 1.65x (128) and 1.53x (64); 3 or 4 units per
+// CTA were equal or slower.  Problems only moderately underfilled (C4's 4
+// heads per GPU, longest item 1.15x the average load; (1, 8, 4096) with 31
+// key tiles) ran 6-18 % slower when split under a looser rule: the fp32
+// partial outputs and the merge cost more than the balance gains.
+#ifndef TK_FWD_SPLIT_UNITS_PER_CTA
+#define TK_FWD_SPLIT_UNITS_PER_CTA 2
+#endif
+constexpr int kSplitUnitsPerCta = TK_FWD_SPLIT_UNITS_PER_CTA;
+
+struct FwdSplitPlan {
+  int split_l = 0, cmax = 0, row0 = 0;
+  long long units = 0;
+  size_t part_bytes = 0, bytes = 0;
+};
+
+template <int D>
+bool plan_fwd_split(int64_t S, int64_t BH, int causal, int sms, FwdSplitPlan& p) {
+  using C = FwdCfg<D>;
+  if (sms <= 0 || S <= 0 || BH <= 0) return false;
+  const long long n_ctiles = (S + C::kT * kTileRows - 1) / (C::kT * kTileRows);
+  const long long n_ntiles = (S + kTileRows - 1) / kTileRows;
+  const long long resident = static_cast<long long>(C::kMinBlocks) * sms;
+  const long long n_pair_units = ((n_ctiles + 1) / 2) * BH;
+  const bool persist_shape = S <= 4 * kTileRows || (causal && (C::kT == 2 || S <= 16 * kTileRows));
+  if (n_ctiles > 1 && n_pair_units >= 2LL * resident && persist_shape) return false;
+  long long work = 0, na_max = 0;
+  for (long long ct = 0; ct < n_ctiles; ++ct) {
+    const long long na = causal ? std::min<long long>(C::kT * ct + 1, n_ntiles) : n_ntiles;
+    work += na;
+    na_max = std::max(na_max, na);
+  }
+  work *= BH;
+  if (na_max < 48 || static_cast<double>(na_max) < 2.0 * static_cast<double>(work) / resident) return false;
+  const long long per = kSplitUnitsPerCta * resident;
+  long long L = std::max<long long>(16, (work + per - 1) / per);
+  long long cmax = (na_max + L - 1) / L;
+  if (cmax > 32) {
+    L = (na_max + 31) / 32;
+    cmax = (na_max + L - 1) / L;
+  }
+  if (cmax < 2) return false;
+  long long units = 0;
+  for (int c = 0; c < cmax; ++c) units += BH * (n_ctiles - split_ct_min(c, static_cast<int>(L), C::kT, causal));
+  if (units > INT32_MAX || BH * cmax * S > INT32_MAX) return false;
+  p.split_l = static_cast<int>(L);
+  p.cmax = static_cast<int>(cmax);
+  p.units = units;
+  p.row0 = causal ? split_ct_min(1, p.split_l, C::kT, causal) * C::kT * kTileRows : 0;
+  p.part_bytes = ((static_cast<size_t>(BH) * cmax * S * D * 4 + 255) / 256) * 256;
+  p.bytes = p.part_bytes + static_cast<size_t>(BH) * cmax * S * 4;
+  return true;
 }
 
 template <int D, bool kBf16, bool kRope>
@@ -643,9 +883,17 @@ int launch_fwd_t(const FwdArgs& a) {
   // beyond which two hardware-scheduled CTAs per SM balance better (9 % at
   // S = 16384).
   const long long resident = static_cast<long long>(C::kMinBlocks) * sms;
+  FwdSplitPlan plan;
+  const bool split = !kRope && a.workspace != nullptr && a.workspace_bytes > 0 &&
+                     plan_fwd_split<D>(a.S, a.BH, a.causal, sms, plan);
+  if (split && a.workspace_bytes < plan.bytes) return kErrInvalidArgument;
   const bool persist_shape =
       a.S <= 4 * kTileRows || (a.causal && (C::kT == 2 || a.S <= 16 * kTileRows));
-  if (n_ctiles > 1 && n_pair_units >= 2LL * resident && persist_shape) {
+  if (split) {
+    mode = kOrderSplit;
+    n_units = plan.units;
+    grid = plan.units;
+  } else if (n_ctiles > 1 && n_pair_units >= 2LL * resident && persist_shape) {
     mode = kOrderPaired;
     n_units = n_pair_units;
     grid = resident;
@@ -663,11 +911,33 @@ int launch_fwd_t(const FwdArgs& a) {
       *a.tm_q, *a.tm_k, *a.tm_v, *a.tm_o, static_cast<uint16_t*>(a.o), a.lse, a.rope_cos, a.rope_sin,
       static_cast<int>(a.S),
       static_cast<int>(a.BH), n_ctiles, a.causal, mode, static_cast<int>(n_units), static_cast<int>(a.D),
-      a.scale_log2, a.timeout_ns, a.status);
-  return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+      a.scale_log2, a.timeout_ns, a.status, split ? plan.split_l : 0, split ? plan.cmax : 0,
+      split ? static_cast<float*>(a.workspace) : nullptr,
+      split ? reinterpret_cast<float*>(static_cast<uint8_t*>(a.workspace) + plan.part_bytes) : nullptr);
+  if (cudaGetLastError() != cudaSuccess) return kErrLaunch;
+  if (split) {
+    const long long n_rows = a.BH * (a.S - plan.row0);
+    const long long blocks = (n_rows * 32 + 255) / 256;
+    if (n_rows > 0) {
+      attn_fwd_combine_kernel<D, kBf16><<<static_cast<unsigned>(blocks), 256, 0, a.stream>>>(
+          static_cast<const float*>(a.workspace),
+          reinterpret_cast<const float*>(static_cast<const uint8_t*>(a.workspace) + plan.part_bytes),
+          static_cast<uint16_t*>(a.o), a.lse, static_cast<int>(a.S), plan.row0, n_rows, a.causal, C::kT,
+          plan.split_l, plan.cmax, static_cast<int>((a.S + kTileRows - 1) / kTileRows), static_cast<int>(a.D));
+      if (cudaGetLastError() != cudaSuccess) return kErrLaunch;
+    }
+  }
+  return kOk;
 }
 
 }  // namespace
+
+size_t attn_fwd_split_bytes(int64_t BH, int64_t S, int64_t D, int causal, int sms) {
+  FwdSplitPlan p;
+  if (D <= 0 || D > 128) return 0;
+  const bool split = (D <= 64) ? plan_fwd_split<64>(S, BH, causal, sms, p) : plan_fwd_split<128>(S, BH, causal, sms, p);
+  return split ? p.bytes : 0;
+}
 
 int launch_attn_fwd(const FwdArgs& a) {
   // head_dim <= 64 runs the 64-column kernel, 64 < head_dim <= 128 the

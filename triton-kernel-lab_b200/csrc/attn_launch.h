@@ -27,6 +27,11 @@ struct FwdArgs {
   // initialisers of the fields above stay valid.
   const float* rope_cos = nullptr;
   const float* rope_sin = nullptr;
+  // Optional scratch for the key-split schedule of problems with too few
+  // work items to fill the device (attn_fwd_split_bytes gives the size; 0
+  // or nullptr: never split).  Unused with RoPE.
+  void* workspace = nullptr;
+  size_t workspace_bytes = 0;
 };
 
 // Forward for 128 < head_dim <= 256 (attn_fwd_d256_sm100.cu): a Q map with
@@ -177,6 +182,9 @@ struct GqaDecodeArgs {
 };
 
 int launch_attn_fwd(const FwdArgs& a);
+// Bytes of workspace the forward's key-split schedule needs for this problem
+// on a device with `sms` SMs (0: the problem is not split).
+size_t attn_fwd_split_bytes(int64_t BH, int64_t S, int64_t D, int causal, int sms);
 int launch_attn_fwd_d256(const FwdD256Args& a);
 int gqa_decode_splits(int64_t B, int64_t Hkv, int64_t L, int sm_count);
 int gqa_decode_keys_per_split(int64_t L, int n_splits);

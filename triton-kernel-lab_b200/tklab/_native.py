@@ -27,6 +27,14 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_float, _vp],
     ),
+    "tk_attn_fwd_ws": (
+        ctypes.c_int,
+        [
+            _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+            _vp, ctypes.c_size_t, _vp,
+        ],
+    ),
+    "tk_attn_fwd_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
     "tk_attn_bwd_pre": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_int, _vp],

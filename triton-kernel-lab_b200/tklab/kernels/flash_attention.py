@@ -27,6 +27,7 @@ Contract differences from the reference, all widenings:
 
 from __future__ import annotations
 
+import functools
 import math
 import os
 import warnings
@@ -229,6 +230,12 @@ def _forward_checked(
     _forward_launch(q, k, v, output, lse_ptr, causal=causal)
 
 
+@functools.lru_cache(maxsize=512)
+def _forward_workspace_bytes(lib, device_index, batch, heads, n_ctx, head_dim, dtype_code, causal) -> int:
+    """Scratch bytes of the key-split forward schedule for this shape on this device (0: not split)."""
+    return int(lib.tk_attn_fwd_workspace_bytes(batch, heads, n_ctx, head_dim, dtype_code, int(causal)))
+
+
 def _forward_launch(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -247,7 +254,13 @@ def _forward_launch(
     batch, heads, n_ctx, head_dim = q.shape
     lib = _native.load()
     with _on_device(q.device):
-        status = lib.tk_attn_fwd(
+        # Problems with too few query tiles for the device run as key-range
+        # chunks merged by a second kernel; their scratch comes from torch's
+        # caching allocator (stream-ordered, so it is freed safely).
+        ws_bytes = _forward_workspace_bytes(lib, q.device.index, batch, heads, n_ctx, head_dim,
+                                            _NATIVE_DTYPE[q.dtype], bool(causal))
+        workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        status = lib.tk_attn_fwd_ws(
             q.data_ptr(),
             k.data_ptr(),
             v.data_ptr(),
@@ -260,9 +273,11 @@ def _forward_launch(
             _NATIVE_DTYPE[q.dtype],
             int(bool(causal)),
             1.0 / math.sqrt(head_dim),
+            None if workspace is None else workspace.data_ptr(),
+            ws_bytes,
             _stream(q),
         )
-    _native.check(status, "tk_attn_fwd")
+    _native.check(status, "tk_attn_fwd_ws")
     _after_launch(q.device)
 
 
