@@ -45,6 +45,7 @@
 // with a caller workspace): chunks of an item's key range in separate CTAs,
 // merged by attn_fwd_combine_kernel.
 #include <algorithm>
+#include <type_traits>
 
 #include "attn_launch.h"
 #include "rope_sm100.cuh"
@@ -751,7 +752,21 @@ __global__ void __launch_bounds__(256)
   const int nch = (na + split_l - 1) / split_l;
   if (nch <= 1) return;
   const size_t base = static_cast<size_t>(bh) * split_cmax * S + m;  // chunk c at base + c S
+  constexpr int kPer = D / 32;  // columns per lane
+  using Vec = typename std::conditional<kPer == 4, float4, float2>::type;
+  // Every load of a group of 8 chunks (and the statistic) is issued before
+  // any of them is used, so a warp waits for one memory latency per group
+  // rather than one per chunk.
+  constexpr int kGroup = 8;
+  Vec v[kGroup];
   const float lc = (lane < nch) ? lse_part[base + static_cast<size_t>(lane) * S] : -INFINITY;
+  auto load_group = [&](int c0) {
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i)
+      if (c0 + i < nch)
+        v[i] = *reinterpret_cast<const Vec*>(o_part + (base + static_cast<size_t>(c0 + i) * S) * D + lane * kPer);
+  };
+  load_group(0);
   float mx = lc;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -759,23 +774,22 @@ __global__ void __launch_bounds__(256)
   float sum = w;
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  constexpr int kPer = D / 32;  // columns per lane
   float acc[kPer];
 #pragma unroll
   for (int e = 0; e < kPer; ++e) acc[e] = 0.0f;
-  for (int c = 0; c < nch; ++c) {
-    const float wc = __shfl_sync(0xffffffffu, w, c);
-    const float* src = o_part + (base + static_cast<size_t>(c) * S) * D + lane * kPer;
-    if constexpr (kPer == 4) {
-      const float4 v = *reinterpret_cast<const float4*>(src);
-      acc[0] += wc * v.x;
-      acc[1] += wc * v.y;
-      acc[2] += wc * v.z;
-      acc[3] += wc * v.w;
-    } else {
-      const float2 v = *reinterpret_cast<const float2*>(src);
-      acc[0] += wc * v.x;
-      acc[1] += wc * v.y;
+  for (int c0 = 0; c0 < nch; c0 += kGroup) {
+    if (c0 > 0) load_group(c0);
+#pragma unroll
+    for (int i = 0; i < kGroup; ++i) {
+      const float wc = __shfl_sync(0xffffffffu, w, (c0 + i) & 31);
+      if (c0 + i < nch) {
+        acc[0] += wc * v[i].x;
+        acc[1] += wc * v[i].y;
+        if constexpr (kPer == 4) {
+          acc[2] += wc * reinterpret_cast<const float4&>(v[i]).z;
+          acc[3] += wc * reinterpret_cast<const float4&>(v[i]).w;
+        }
+      }
     }
   }
   const float inv = 1.0f / sum;
