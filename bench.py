@@ -962,7 +962,9 @@ def main() -> None:
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--config", choices=tuple(CONFIGS), default="c3")
     parser.add_argument("--seed", type=int, default=0)
-    parser.add_argument("--e2e-steps", type=int, default=10)
+    # Enough timed steps that the pipeline's fill and drain (one extra
+    # upload and download) weigh little against the steady-state rate.
+    parser.add_argument("--e2e-steps", type=int, default=30)
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
