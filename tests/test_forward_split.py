@@ -6,7 +6,7 @@ forward's time.  ``tk_attn_fwd_workspace_bytes`` reports scratch for them,
 and ``tk_attn_fwd_ws`` then runs each long query tile as chunks of its key
 range (fp32 partial outputs and base-2 log-sum-exps in the scratch) merged by
 a second kernel.  These tests run such shapes (causal and not, fp16 and
-bf16, head_dim 64 / 96 / 128, ragged sequence lengths) through the C ABI
+bf16, head_dim 40 / 64 / 72 / 96 / 128, ragged sequence lengths) through the C ABI
 into NaN-prefilled outputs and compare:
 
 * with the CPU oracle (``chunked_reference``) on the first and last slabs, at
@@ -52,6 +52,8 @@ SPLIT_CASES = [
     (1, 2, 8000, 96, torch.bfloat16, True),
     (1, 1, 7000, 64, torch.float16, False),
     (1, 1, 12300, 128, torch.float16, True),
+    (1, 1, 7000, 40, torch.bfloat16, True),
+    (1, 2, 8192, 72, torch.float16, False),
 ]
 
 

@@ -275,12 +275,12 @@ __device__ __forceinline__ void fwd_split_decode(int u, int BH, int n_ctiles, in
 
 // split_item: the CTA's (bh, ct, chunk) in shared memory, decoded by
 // fwd_split_decode (split mode only).
-template <int kT>
+template <int kT, bool kSplit>
 __device__ __forceinline__ FwdItem fwd_item(int u, int sub, int BH, int n_ctiles, int n_ntiles, int causal,
                                             int mode, int split_l, const int* split_item) {
   FwdItem f;
   f.chunk = 0;
-  if (mode == kOrderSplit) {
+  if constexpr (kSplit) {
     f.bh = split_item[0];
     f.ct = split_item[1];
     f.chunk = split_item[2];
@@ -289,7 +289,7 @@ __device__ __forceinline__ FwdItem fwd_item(int u, int sub, int BH, int n_ctiles
   }
   const int na = causal ? min(kT * f.ct + 1, n_ntiles) : n_ntiles;
   const int nb = causal ? min(kT * f.ct + kT, n_ntiles) : n_ntiles;
-  if (mode == kOrderSplit) {
+  if constexpr (kSplit) {
     f.j0 = f.chunk * split_l;
     const int ea = min(f.j0 + split_l, na);
     const int eb = (ea == na) ? nb : ea;
@@ -312,7 +312,9 @@ __device__ __forceinline__ FwdItem fwd_item(int u, int sub, int BH, int n_ctiles
 // otherwise wait for S(0).  K arrives rotated (the caller rotates it once:
 // every CTA streams every K tile, so rotating K here would repeat the work
 // once per query tile).
-template <int D, bool kBf16, bool kRope>
+// kSplit: the key-split schedule (mode kOrderSplit, chunk partials to
+// o_part / lse_part); the regular kernels carry none of its code.
+template <int D, bool kBf16, bool kRope, bool kSplit>
 __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -366,7 +368,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
     mbar_init(&q_rot[0], 4);  // the four warps of softmax warpgroup x
     mbar_init(&q_rot[1], 4);
     ctl->abort = 0;
-    if (mode == kOrderSplit) fwd_split_decode(blockIdx.x, BH, n_ctiles, causal, C::kT, split_l, split_item);
+    if constexpr (kSplit) fwd_split_decode(blockIdx.x, BH, n_ctiles, causal, C::kT, split_l, split_item);
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -394,7 +396,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
       for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x) {
         const int n_sub = fwd_unit_items(u, n_ctiles, mode);
         for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
-          const FwdItem f = fwd_item<C::kT>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
+          const FwdItem f = fwd_item<C::kT, kSplit>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
           const int bh = f.bh;
           const int m0 = f.ct * C::kT * kTileRows;
           const int n_kv_b = f.n_b;
@@ -475,7 +477,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
         const int n_sub = fwd_unit_items(u, n_ctiles, mode);
         for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
           // Key tiles are counted from the item's first one (f.j0).
-          const FwdItem f = fwd_item<C::kT>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
+          const FwdItem f = fwd_item<C::kT, kSplit>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
           const int n_kv_a = f.n_a;
           const int n_kv_b = f.n_b;
           // S_x(0) overwrites the previous item's P_x, whose P.V was issued
@@ -569,7 +571,7 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
       for (int sub = 0; ok && sub < n_sub; ++sub, ++it) {
         int bh, m0, n_kv_x, n_first;
         {
-          const FwdItem f = fwd_item<C::kT>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
+          const FwdItem f = fwd_item<C::kT, kSplit>(u, sub, BH, n_ctiles, n_ntiles, causal, mode, split_l, split_item);
           bh = f.bh;
           m0 = f.ct * C::kT * kTileRows;
           n_kv_x = (x == 0) ? f.n_a : f.n_b;
@@ -630,8 +632,8 @@ __global__ void __launch_bounds__(FwdCfg<D>::kThreads, FwdCfg<D>::kMinBlocks)
         const bool row_ok = row_g < S;
         // (Split state re-derived here rather than held through the key loop.)
         const int n_kv_item_a = causal ? min(m0 / kTileRows + 1, n_ntiles) : n_ntiles;
-        const bool split_out = mode == kOrderSplit && n_kv_item_a > split_l;
-        if (split_out) {
+        const bool split_out = kSplit && n_kv_item_a > split_l;
+        if (kSplit && split_out) {
           // One chunk of a split item: O_x / row_sum of this chunk in fp32
           // (all D columns; those past the true head_dim are zero) and its
           // base-2 log-sum-exp, for attn_fwd_combine_kernel.
@@ -874,11 +876,12 @@ template <int D, bool kBf16, bool kRope>
 int launch_fwd_t(const FwdArgs& a) {
   using C = FwdCfg<D>;
   static_assert(C::kSmemBytes <= 232448, "forward shared memory exceeds the sm_100 limit");
-  auto kern = attn_fwd_kernel<D, kBf16, kRope>;
+  auto kern_regular = attn_fwd_kernel<D, kBf16, kRope, false>;
+  auto kern_split = attn_fwd_kernel<D, kBf16, false, true>;
   // The setmaxnreg split inside the kernel assumes exactly C::kLaunchRegs
   // registers per thread at launch; a build that differs is refused.
   int sms = 0;
-  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern), C::kSmemBytes, C::kLaunchRegs, &sms))
+  if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern_regular), C::kSmemBytes, C::kLaunchRegs, &sms))
     return rc;
   const int n_ctiles = static_cast<int>((a.S + C::kT * kTileRows - 1) / (C::kT * kTileRows));
   const long long n_items = static_cast<long long>(n_ctiles) * a.BH;
@@ -901,6 +904,11 @@ int launch_fwd_t(const FwdArgs& a) {
   const bool split = !kRope && a.workspace != nullptr && a.workspace_bytes > 0 &&
                      plan_fwd_split<D>(a.S, a.BH, a.causal, sms, plan);
   if (split && a.workspace_bytes < plan.bytes) return kErrInvalidArgument;
+  if (split) {
+    if (int rc = prepare_kernel(reinterpret_cast<const void*>(kern_split), C::kSmemBytes, C::kLaunchRegs, nullptr))
+      return rc;
+  }
+  auto kern = split ? kern_split : kern_regular;
   const bool persist_shape =
       a.S <= 4 * kTileRows || (a.causal && (C::kT == 2 || a.S <= 16 * kTileRows));
   if (split) {
