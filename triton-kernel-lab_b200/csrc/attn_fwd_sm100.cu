@@ -45,7 +45,13 @@
 // with a caller workspace): chunks of an item's key range in separate CTAs,
 // merged by attn_fwd_combine_kernel.
 #include <algorithm>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <queue>
+#include <tuple>
 #include <type_traits>
+#include <vector>
 
 #include "attn_launch.h"
 #include "rope_sm100.cuh"
@@ -812,27 +818,62 @@ __global__ void __launch_bounds__(256)
 // The key-split schedule.  Used only when the regular one would not be
 // persistent, its longest item has at least 48 key tiles and at least twice
 // the average load of a resident CTA (the device is less than half busy on
-// average while that item runs): chunks of split_l key tiles (at least 16,
-// sized so that there are about kSplitUnitsPerCta chunks' worth of tile-A
-// key tiles per resident CTA), at most 32 chunks per item.  Measured on one
-// B200 (split against unsplit, bf16, L2 flushed, interleaved): (B, H, S) =
-// (1, 2, 8192) causal 1.94x, (1, 4, 8192) causal 1.17x, (1, 2, 16384)
-// causal 1.41x (head_dim 128) and 1.34x (64), (1, 1, 16384) non-causal
-// 1.53x, (1, 1, 32768) causal 1.65x (128) and 1.53x (64); 3 or 4 units per
-// CTA were equal or slower.  Problems only moderately underfilled (C4's 4
+// average while that item runs): chunks of split_l key tiles, the length
+// chosen by simulating the schedule (split_makespan), at most 32 chunks per
+// item.  Measured on one B200 with a fixed length (about two chunks' worth
+// of tile-A key tiles per resident CTA, at least 16; split against unsplit,
+// bf16, L2 flushed, interleaved): (B, H, S) = (1, 2, 8192) causal 1.94x,
+// (1, 4, 8192) causal 1.17x, (1, 2, 16384) causal 1.41x (head_dim 128) and
+// 1.34x (64), (1, 1, 16384) non-causal 1.53x, (1, 1, 32768) causal 1.65x
+// (128) and 1.53x (64); 3 or 4 chunks' worth per CTA were equal or slower,
+// and (1, 4, 8192)'s 320 chunks of 16 tiles took three full rounds of the
+// 148 SMs, which the simulated choice avoids.  Problems only moderately underfilled (C4's 4
 // heads per GPU, longest item 1.15x the average load; (1, 8, 4096) with 31
 // key tiles) ran 6-18 % slower when split under a looser rule: the fp32
 // partial outputs and the merge cost more than the balance gains.
-#ifndef TK_FWD_SPLIT_UNITS_PER_CTA
-#define TK_FWD_SPLIT_UNITS_PER_CTA 2
-#endif
-constexpr int kSplitUnitsPerCta = TK_FWD_SPLIT_UNITS_PER_CTA;
 
 struct FwdSplitPlan {
   int split_l = 0, cmax = 0, row0 = 0;
   long long units = 0;
   size_t part_bytes = 0, bytes = 0;
 };
+
+// A chunk's fixed cost in key-tile times: the CTA's prologue (TMEM and
+// barrier set-up, Q load, pipeline fill), its fp32 partial store and its
+// share of the merge.  Fitted to four measured split schedules (chunks of
+// 16 and 28 key tiles at head_dim 128), which it reproduces within three
+// tile times.
+constexpr double kChunkOverheadTiles = 7.5;
+
+// Estimated duration, in key-tile times, of the split schedule with chunks
+// of L key tiles: its units in the kernel's launch order (chunk level, then
+// slab, then query-tile group from the heaviest), each costing its tile-B
+// key tiles plus kChunkOverheadTiles, handed to whichever of the `resident`
+// CTA slots frees first, as the hardware does with a grid larger than the
+// device.
+double split_makespan(long long n_ctiles, long long n_ntiles, long long BH, int causal, int kT, long long L,
+                      long long cmax, long long resident) {
+  std::priority_queue<double, std::vector<double>, std::greater<double>> slots;
+  for (long long i = 0; i < resident; ++i) slots.push(0.0);
+  double makespan = 0.0;
+  for (long long c = 0; c < cmax; ++c) {
+    const long long ct_lo = split_ct_min(static_cast<int>(c), static_cast<int>(L), kT, causal);
+    for (long long bh = 0; bh < BH; ++bh) {
+      for (long long ct = n_ctiles - 1; ct >= ct_lo; --ct) {
+        const long long na = causal ? std::min<long long>(kT * ct + 1, n_ntiles) : n_ntiles;
+        const long long nb = causal ? std::min<long long>(kT * ct + kT, n_ntiles) : n_ntiles;
+        const long long j0 = c * L;
+        const long long ea = std::min(j0 + L, na);
+        const long long eb = (ea == na) ? nb : ea;
+        const double t = slots.top() + static_cast<double>(eb - j0) + kChunkOverheadTiles;
+        slots.pop();
+        slots.push(t);
+        makespan = std::max(makespan, t);
+      }
+    }
+  }
+  return makespan;
+}
 
 template <int D>
 bool plan_fwd_split(int64_t S, int64_t BH, int causal, int sms, FwdSplitPlan& p) {
@@ -852,14 +893,37 @@ bool plan_fwd_split(int64_t S, int64_t BH, int causal, int sms, FwdSplitPlan& p)
   }
   work *= BH;
   if (na_max < 48 || static_cast<double>(na_max) < 2.0 * static_cast<double>(work) / resident) return false;
-  const long long per = kSplitUnitsPerCta * resident;
-  long long L = std::max<long long>(16, (work + per - 1) / per);
-  long long cmax = (na_max + L - 1) / L;
-  if (cmax > 32) {
-    L = (na_max + 31) / 32;
-    cmax = (na_max + L - 1) / L;
+  // Chunk length: the one whose simulated schedule ends first, among
+  // lengths from 12 key tiles (shorter chunks pay their fixed cost too
+  // often) to four times the average load per resident CTA, with at most
+  // 32 chunks per item; ties go to the longer chunk (fewer partials).
+  // Planned once per shape and device width.
+  static std::mutex mu;
+  static std::map<std::tuple<int64_t, int64_t, int, int>, std::pair<long long, long long>> cache;
+  long long L = 0, cmax = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(S, BH, causal, sms);
+    auto it = cache.find(key);
+    if (it == cache.end()) {
+      const long long hi = std::min<long long>(na_max - 1, std::max<long long>(12, 4 * work / resident + 1));
+      double best = 0.0;
+      for (long long l = hi; l >= 12; --l) {
+        const long long cm = (na_max + l - 1) / l;
+        if (cm > 32 || cm < 2) continue;
+        const double t = split_makespan(n_ctiles, n_ntiles, BH, causal, C::kT, l, cm, resident);
+        if (L == 0 || t < best) {
+          best = t;
+          L = l;
+          cmax = cm;
+        }
+      }
+      it = cache.emplace(key, std::make_pair(L, cmax)).first;
+    }
+    L = it->second.first;
+    cmax = it->second.second;
   }
-  if (cmax < 2) return false;
+  if (L == 0 || cmax < 2) return false;
   long long units = 0;
   for (int c = 0; c < cmax; ++c) units += BH * (n_ctiles - split_ct_min(c, static_cast<int>(L), C::kT, causal));
   if (units > INT32_MAX || BH * cmax * S > INT32_MAX) return false;
