@@ -42,6 +42,11 @@ def load_selftest_lib():
     lib.tk_selftest_exp2_fma.argtypes = [vp, vp, ctypes.c_int64, vp]
     lib.tk_selftest_status.restype = c_int
     lib.tk_selftest_status.argtypes = [ctypes.POINTER(c_int), vp]
+    i64 = ctypes.c_int64
+    lib.tk_selftest_fwd_split_plan.restype = c_int
+    lib.tk_selftest_fwd_split_plan.argtypes = [i64, i64, i64, c_int, c_int, ctypes.POINTER(i64)]
+    lib.tk_selftest_fwd_split_decode.restype = None
+    lib.tk_selftest_fwd_split_decode.argtypes = [c_int, c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]
     return lib
 
 

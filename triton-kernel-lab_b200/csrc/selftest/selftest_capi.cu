@@ -6,6 +6,7 @@
 #include <mutex>
 
 #include "../../../include/tklab_attn.h"
+#include "../attn_fwd_split_plan.h"
 #include "../sm100_primitives.cuh"
 #include "tklab_selftest.h"
 #include "tklab_selftest_impl.h"
@@ -116,6 +117,24 @@ int tk_selftest_exp2_fma(const float* x, float* y, int64_t n, void* stream) {
   if (x == nullptr || y == nullptr || n <= 0) return tk::kErrInvalidArgument;
   if ((reinterpret_cast<uintptr_t>(x) & 3u) || (reinterpret_cast<uintptr_t>(y) & 3u)) return tk::kErrMisaligned;
   return tk::launch_exp2_fma_pair(x, y, n, static_cast<cudaStream_t>(stream));
+}
+
+int tk_selftest_fwd_split_plan(int64_t bh, int64_t seq, int64_t head_dim, int causal, int sms, int64_t* out) {
+  if (out == nullptr || head_dim <= 0 || head_dim > 128) return 0;
+  const tk::FwdKernelShape k = tk::fwd_kernel_shape(head_dim);
+  tk::FwdSplitPlan p;
+  if (!tk::plan_fwd_split_impl(k.kT, k.min_blocks, k.width, seq, bh, causal ? 1 : 0, sms, p)) return 0;
+  out[0] = p.split_l;
+  out[1] = p.cmax;
+  out[2] = p.units;
+  out[3] = p.row0;
+  out[4] = static_cast<int64_t>(p.bytes);
+  out[5] = k.kT;
+  return 1;
+}
+
+void tk_selftest_fwd_split_decode(int u, int bh, int n_ctiles, int causal, int kt, int split_l, int* out) {
+  if (out != nullptr) tk::fwd_split_decode(u, bh, n_ctiles, causal, kt, split_l, out);
 }
 
 int tk_selftest_status(int* status_out, void* stream) {

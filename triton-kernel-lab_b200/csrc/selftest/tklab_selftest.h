@@ -30,6 +30,20 @@ TKS_API int tk_selftest_umma(const void* a, const void* b, float* c, int mode, i
  * (exp2_fma_pair), evaluated on x[i], i < n.  x and y are device fp32. */
 TKS_API int tk_selftest_exp2_fma(const float* x, float* y, int64_t n, void* stream);
 
+/* Host-side view of the forward's key-split schedule
+ * (csrc/attn_fwd_split_plan.h, the code the attention library runs), for
+ * CPU tests.  tk_selftest_fwd_split_plan: 1 when a (bh, seq, head_dim,
+ * causal) forward on a device with `sms` SMs is split, with out[0..5] =
+ * chunk length in key tiles, chunks per item at most, units (CTAs), first
+ * row of a multi-chunk item, workspace bytes, query tiles per work item;
+ * 0 when it is not split.  No device is touched. */
+TKS_API int tk_selftest_fwd_split_plan(int64_t bh, int64_t seq, int64_t head_dim, int causal, int sms,
+                                       int64_t* out);
+
+/* The forward kernel's decode of split unit u: out[0..2] = slab, query-tile
+ * group, chunk.  Host code only. */
+TKS_API void tk_selftest_fwd_split_decode(int u, int bh, int n_ctiles, int causal, int kt, int split_l, int* out);
+
 /* Synchronise `stream`, then read and clear this library's device status
  * word (the first error a probe kernel recorded). */
 TKS_API int tk_selftest_status(int* status_out, void* stream);
