@@ -227,7 +227,9 @@ def _forward_checked(
             raise ValueError("attention log-sum-exp buffer must be contiguous float32 BxHxN")
         assert_int32_addressable(softmax_lse, name="log-sum-exp buffer")
         lse_ptr = softmax_lse.data_ptr()
-    _forward_launch(q, k, v, output, lse_ptr, causal=causal)
+    # Launches into caller buffers allocate nothing, as the reference's
+    # launcher: no key-split scratch on this path.
+    _forward_launch(q, k, v, output, lse_ptr, causal=causal, key_split=False)
 
 
 @functools.lru_cache(maxsize=512)
@@ -244,21 +246,28 @@ def _forward_launch(
     lse_ptr: int | None,
     *,
     causal: bool,
+    key_split: bool,
 ) -> None:
     """The library call itself, for a validated Q/K/V and buffers whose metadata is known to match.
 
-    ``_forward_checked`` reaches it after checking caller-supplied buffers;
+    ``_forward_checked`` reaches it after checking caller-supplied buffers
+    (``key_split=False``: allocation-free, like the reference's launcher);
     ``_attention`` and the autograd forward call it directly with buffers
-    they allocated themselves (``empty_like(q)`` and a float32 BxHxN LSE).
+    they allocated themselves (``empty_like(q)`` and a float32 BxHxN LSE),
+    and with ``key_split=True``: problems with too few query tiles for the
+    device then run as key-range chunks merged by a second kernel, with
+    scratch from torch's caching allocator.
     """
     batch, heads, n_ctx, head_dim = q.shape
     lib = _native.load()
     with _on_device(q.device):
-        # Problems with too few query tiles for the device run as key-range
-        # chunks merged by a second kernel; their scratch comes from torch's
-        # caching allocator (stream-ordered, so it is freed safely).
-        ws_bytes = _forward_workspace_bytes(lib, q.device.index, batch, heads, n_ctx, head_dim,
-                                            _NATIVE_DTYPE[q.dtype], bool(causal))
+        # Scratch of the key-split schedule, from torch's caching allocator
+        # (stream-ordered, so it is freed safely); 0 when the problem fills
+        # the device or the caller wants no allocation.
+        ws_bytes = 0
+        if key_split:
+            ws_bytes = _forward_workspace_bytes(lib, q.device.index, batch, heads, n_ctx, head_dim,
+                                                _NATIVE_DTYPE[q.dtype], bool(causal))
         workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
         status = lib.tk_attn_fwd_ws(
             q.data_ptr(),
@@ -420,7 +429,7 @@ class _FlashAttentionFunction(torch.autograd.Function):
         output = torch.empty_like(q)
         batch, heads, n_ctx, _ = q.shape
         softmax_lse = torch.empty((batch, heads, n_ctx), dtype=torch.float32, device=q.device)
-        _forward_launch(q, k, v, output, softmax_lse.data_ptr(), causal=causal)
+        _forward_launch(q, k, v, output, softmax_lse.data_ptr(), causal=causal, key_split=True)
         ctx.save_for_backward(q, k, v, output, softmax_lse)
         ctx.causal = causal
         return output
@@ -452,7 +461,7 @@ def _attention(
     needs_grad = torch.is_grad_enabled() and any(tensor.requires_grad for tensor in (q, k, v))
     if not needs_grad:
         output = torch.empty_like(q)
-        _forward_launch(q, k, v, output, None, causal=causal)
+        _forward_launch(q, k, v, output, None, causal=causal, key_split=True)
         return output
     result = _FlashAttentionFunction.apply(q, k, v, causal)
     return cast(torch.Tensor, result)
