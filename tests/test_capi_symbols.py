@@ -61,6 +61,31 @@ def test_forward_rejects_bad_arguments_before_launch(kwargs: dict, status: int) 
     assert _native.load().tk_attn_fwd(*args.values()) == status
 
 
+@pytest.mark.parametrize(
+    ("kwargs", "status"),
+    [
+        ({"q": None}, 1),
+        ({"head_dim": 100}, 2),
+        ({"scale": float("nan")}, 1),
+        ({"o": 0x4004}, 3),
+        ({"workspace": 0x5010, "ws_bytes": 4096}, 3),  # scratch must be 256-byte aligned
+    ],
+)
+def test_forward_with_scratch_rejects_bad_arguments_before_launch(kwargs: dict, status: int) -> None:
+    args = {"q": 0x1000, "k": 0x2000, "v": 0x3000, "o": 0x4000, "lse": None, "batch": 1, "heads": 2,
+            "seq": 128, "head_dim": 64, "dtype": 0, "causal": 0, "scale": 0.125, "workspace": None,
+            "ws_bytes": 0, "stream": None}
+    args.update(kwargs)
+    assert _native.load().tk_attn_fwd_ws(*args.values()) == status
+
+
+def test_forward_scratch_size_of_invalid_shapes_is_zero() -> None:
+    lib = _native.load()
+    assert lib.tk_attn_fwd_workspace_bytes(0, 2, 8192, 128, 1, 1) == 0
+    assert lib.tk_attn_fwd_workspace_bytes(1, 2, 8192, 100, 1, 1) == 0
+    assert lib.tk_attn_fwd_workspace_bytes(1, 2, 8192, 128, 7, 1) == 0
+
+
 @pytest.mark.parametrize("head_dim", [136, 256])
 def test_deterministic_backward_rejects_wide_heads(head_dim: int) -> None:
     """136..256 have a default backward only: the deterministic entries refuse them as unsupported."""
